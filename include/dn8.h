@@ -1,0 +1,81 @@
+/* dn8.h -- C ABI of libdn8b200.so, the Blackwell (sm_100a) INT8 DenseNet169 encoder.
+ *
+ * Two levels, both plain C (pointers, sizes, integer status; no exceptions cross the ABI):
+ *
+ * 1. Kernel level. The reference binds each INT8 kernel by name through its ctypes driver-API
+ *    wrapper `cudart.Function.launch(grid, block, [struct], stream, shared)`
+ *    (src/knee/cudart.py:138-153) with a by-value argument struct (`KArg`
+ *    src/knee/dense8s_kernels.cu:147-158, `C2Arg` :1936-1942). Here each kernel family is one
+ *    host function taking an argument struct of the same meaning plus the caller's stream; the
+ *    library picks grid, block and shared memory itself. All pointers are DEVICE pointers. The
+ *    weight / scale tables are the reference pack tables (`kernel_params`,
+ *    src/knee/dense8s.py:457-519) unchanged.
+ *
+ * 2. Engine level. Replaces `Dense8SEncoder` (src/knee/dense8s.py:944-1488): one handle per
+ *    (GPU, seed) owns the device copies of the pack tables and the block arenas; `dn8_forward`
+ *    enqueues one whole pass (stem, 82 dense layers, 3 transitions, pooling + head) on the
+ *    caller's stream without host synchronisation or allocation, so it can be captured in a CUDA
+ *    graph. A handle is not thread-safe; distinct handles are independent.
+ *
+ * Status codes: DN8_OK, DN8_EINVAL (bad argument or unsupported geometry; the reference raises
+ * ValueError), DN8_ECUDA (CUDA runtime error; reference `cudart.CudaError`), DN8_EDEVICE (a kernel
+ * reported an error through its error word: a bounded device-side wait gave up). The last error
+ * message of a handle (or of the calling thread, for the kernel level) is dn8_last_error().
+ */
+#ifndef DN8_H
+#define DN8_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DN8_OK 0
+#define DN8_EINVAL 1
+#define DN8_ECUDA 2
+#define DN8_EDEVICE 3
+
+typedef void* dn8_stream; /* a cudaStream_t; NULL = legacy default stream */
+
+/* ---- kernel level -------------------------------------------------------------------------- */
+
+/* conv1 of dense layer (b, l): replaces `conv1_w64_pl(KArg)` / `conv1_u*(KArg)` (reference
+ * src/knee/dense8s_kernels.cu:479-627, launched by `Dense8SEncoder._c1_item` src/knee/dense8s.py:1205-1240).
+ * u = prologue(q) per channel, acc = sum_c W[o,c] u_c (int32), out = rint(255 sat(g_o acc + d_o)).
+ * Store: in0 [N][G0][HW][32] int8, seg [L][N][HW][32] int8 (groups G0.. read from seg).
+ * Output: the u8 bottleneck as 8 planes of 16 channels, [8][N*HW][16]. */
+typedef struct dn8_conv1_args {
+    const int8_t* in0;
+    const int8_t* seg;
+    const int8_t* w;    /* L*_w1: [G][128][32] int8 */
+    const void* ab;     /* prologue table: L*_abh [G*16][4] fp16 (prologue_f16 = 1) or L*_ab [G*32][2] float */
+    const float* gd;    /* L*_gdu: [128][2] float */
+    uint8_t* out;       /* [8][N*HW][16] */
+    int32_t* err;       /* device error word (0 = none) or NULL */
+    int32_t G0, G, N, HW;
+    int32_t prologue_f16;
+} dn8_conv1_args;
+int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream);
+
+/* conv2 of dense layer (b, l): replaces `conv2_t8x32_pl` / `conv2_t16x16_pl(C2Arg)` (reference
+ * :2679-2832, `_c2_item` src/knee/dense8s.py:1274-1290). 3x3 pad-1 conv 128 -> 32 on the u8
+ * bottleneck, q = rint(clamp(acc * sc_o, +-127)) written into the store slot [N][HW][32].
+ * Requires W <= 128. */
+typedef struct dn8_conv2_args {
+    const uint8_t* x;   /* bottleneck planes [8][N*H*W][16] */
+    const int8_t* w;    /* L*_w2k: [4][9][32][32] int8 (channel block, tap, out, in) */
+    const float* sc;    /* L*_c2u: [32] float */
+    int8_t* out;        /* store slot [N][H*W][32] */
+    int32_t* err;
+    int32_t N, H, W;
+} dn8_conv2_args;
+int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream);
+
+const char* dn8_last_error(void);   /* message of the calling thread's last failed call */
+int dn8_device_sms(int device);     /* SM count used to size persistent grids (0 on error) */
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DN8_H */

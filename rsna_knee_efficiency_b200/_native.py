@@ -1,0 +1,59 @@
+"""ctypes binding of libdn8b200.so (include/dn8.h). No fallback: if the library or a GPU is missing,
+every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libdn8b200.so")
+DN8_OK, DN8_EINVAL, DN8_ECUDA, DN8_EDEVICE = 0, 1, 2, 3
+P, I32 = ctypes.c_void_p, ctypes.c_int32
+
+
+class Conv1Args(ctypes.Structure):
+    _fields_ = [("in0", P), ("seg", P), ("w", P), ("ab", P), ("gd", P), ("out", P), ("err", P),
+                ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("prologue_f16", I32)]
+
+
+class Conv2Args(ctypes.Structure):
+    _fields_ = [("x", P), ("w", P), ("sc", P), ("out", P), ("err", P),
+                ("N", I32), ("H", I32), ("W", I32)]
+
+
+EXPORTS = {
+    "dn8_conv1": ([ctypes.POINTER(Conv1Args), P], ctypes.c_int),
+    "dn8_conv2": ([ctypes.POINTER(Conv2Args), P], ctypes.c_int),
+    "dn8_last_error": ([], ctypes.c_char_p),
+    "dn8_device_sms": ([ctypes.c_int], ctypes.c_int),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded library (built in-tree by `build.py`); raises if it is missing."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with "
+                               "`python -m rsna_knee_efficiency_b200.build` (no CPU fallback)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in EXPORTS.items():
+            fn = getattr(handle, name)
+            fn.argtypes, fn.restype = args, res
+        _lib = handle
+    return _lib
+
+
+class Dn8Error(RuntimeError):
+    pass
+
+
+def check(status: int, what: str) -> None:
+    if status == DN8_OK:
+        return
+    msg = lib().dn8_last_error().decode(errors="replace")
+    if status == DN8_EINVAL:
+        raise ValueError(f"{what}: {msg}")
+    raise Dn8Error(f"{what} (status {status}): {msg}")

@@ -1,0 +1,244 @@
+// conv2.cu -- dense-layer conv2 on sm_100a: 3x3 pad-1 conv 128 -> 32 on the u8 bottleneck,
+// int8 requantisation straight into the block store slot.
+//
+// Formulation ("dx in N"): a tile is Rt = 128 / W full image rows (128 pixels, W <= 128). For
+// each kernel row dy and channel block c (12 K steps of 32 channels) one
+// tcgen05.mma M128 N96 K32 multiplies the tile's pixels shifted by dy rows (A: a shifted view of
+// the bottleneck rows held in shared memory, no copy) by the weights of the three taps dx of
+// that row stacked along N (96 = 3 dx x 32 outputs):
+//     D[p][dx, o] = sum_{dy, c} W[dy, dx][o][c] * X[y(p) + dy - 1, x(p)][c].
+// The epilogue adds the three column taps: out[p][o] = D[p-1][0, o] + D[p][1, o] + D[p+1][2, o]
+// (neighbours through warp shuffles, zero outside the row), so no column halo is ever loaded.
+// One 5-D TMA load per tile brings the 8 bottleneck planes x (Rt + 2) rows; rows outside the
+// image arrive zero-filled (the convolution's zero padding).
+// Warp roles: warp 0 TMEM owner + TMA producer, warp 1 MMA issuer, warps 2-9 epilogue (warp w
+// reads TMEM lanes 32*(w%4).. and 16 of the 32 outputs).
+#include "dn8_common.cuh"
+#include "dn8_kernels.h"
+
+namespace dn8 {
+
+constexpr int C2_STAGES = 3;
+constexpr int C2_THREADS = 320;
+constexpr int C2_W_BYTES = 36864;            // [dy][cblk][2 halves][96 rows][16 B]
+
+static inline int c2_rows_per_tile(int H, int W) {
+    int rt = 128 / W;
+    return rt < H ? rt : H;
+}
+// A stage holds 8 planes of (Rt + 2) rows; the MMA of the last plane reads 128 rows from row 2,
+// which can run past the plane when Rt * W < 128 (junk rows): the stage is sized to cover it.
+static inline size_t c2_stage_bytes(int Rt, int W) {
+    const size_t pl = static_cast<size_t>(Rt + 2) * W * 16;
+    const size_t need = 7 * pl + static_cast<size_t>(2 * W + 128) * 16;
+    const size_t b = need > 8 * pl ? need : 8 * pl;
+    return ((b + 1023) / 1024) * 1024;
+}
+size_t conv2_smem_bytes(int H, int W) {
+    const int Rt = c2_rows_per_tile(H, W);
+    return 1024 + C2_W_BYTES + C2_STAGES * c2_stage_bytes(Rt, W) + 128 + 2 * 2 * 4 * 2 * 16 * 4 +
+           8 * (2 * C2_STAGES + 8) + 16;
+}
+
+__global__ void __launch_bounds__(C2_THREADS, 1)
+conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, int Rt, uint32_t stage_bytes) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sW = smem;
+    uint8_t* sX = smem + C2_W_BYTES;                       // stages, 1024-aligned (36864 = 36 * 1024)
+    float* sSc = reinterpret_cast<float*>(sX + C2_STAGES * stage_bytes);
+    int32_t* xb = reinterpret_cast<int32_t*>(sSc + 32);    // [2 acc][2 ch][4 quad][2][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(xb + 2 * 2 * 4 * 2 * 16);
+    uint64_t* empty = full + C2_STAGES;
+    uint64_t* accf = empty + C2_STAGES;
+    uint64_t* acce = accf + 2;
+    uint64_t* xbar = acce + 2;                             // [2 acc][2 ch]: neighbour exchange
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(xbar + 4);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = a.H, W = a.W;
+    const int tpi = (H + Rt - 1) / Rt;
+    const int ntiles = a.N * tpi;
+    const int my_tiles = static_cast<int>(blockIdx.x) < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const uint32_t PL = static_cast<uint32_t>((Rt + 2) * W * 16);     // one plane of a stage
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C2_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int k = 0; k < 2; ++k) {
+            mbar_init(&accf[k], 1);
+            mbar_init(&acce[k], 8);
+        }
+        for (int k = 0; k < 4; ++k) mbar_init(&xbar[k], 4);
+        *s_abort = 0;
+        mbar_fence_init();
+        prefetch_tensormap(&tmap);
+    }
+    // weights: w2k [cblk][tap][o][32] -> [dy][cblk][half][dx * 32 + o][16]
+    for (int q = threadIdx.x; q < C2_W_BYTES / 16; q += C2_THREADS) {
+        const int hh = q & 1, o = (q >> 1) & 31, tap = (q >> 6) % 9, blk = (q >> 6) / 9;
+        const int dy = tap / 3, dx = tap % 3;
+        *reinterpret_cast<uint4*>(sW + ((dy * 4 + blk) * 2 + hh) * 1536 + (dx * 32 + o) * 16) =
+            __ldg(reinterpret_cast<const uint4*>(a.w) + q);
+    }
+    if (threadIdx.x < 32) sSc[threadIdx.x] = a.sc[threadIdx.x];
+    fence_async_smem();
+    if (warp == 0) tmem_alloc(s_tmem, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int t = 0; t < my_tiles; ++t) {
+                const int s = t % C2_STAGES;
+                if (!mbar_wait(&empty[s], ((t / C2_STAGES) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+                const int tile = blockIdx.x + t * gridDim.x;
+                const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
+                mbar_expect_tx(&full[s], 8u * PL);
+                tma_load_5d(sX + s * stage_bytes, &tmap, &full[s], 0, 0, y0 - 1, n, 0);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_u8s8(128, 96);
+            const uint32_t x0 = smem_u32(sX), w0 = smem_u32(sW);
+            for (int t = 0; t < my_tiles; ++t) {
+                const int acc = t & 1, s = t % C2_STAGES;
+                if (!mbar_wait(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+                tc_fence_after();
+                if (!mbar_wait(&full[s], (t / C2_STAGES) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
+                tc_fence_after();
+                const uint32_t xs = x0 + s * stage_bytes;
+#pragma unroll
+                for (int dy = 0; dy < 3; ++dy)
+#pragma unroll
+                    for (int cb = 0; cb < 4; ++cb) {
+                        const uint64_t ad = sdesc(xs + 2 * cb * PL + dy * W * 16, PL, 128, LAYOUT_NONE);
+                        const uint64_t bd = sdesc(w0 + (dy * 4 + cb) * 3072, 1536, 128, LAYOUT_NONE);
+                        umma_u8s8(tmem + acc * 128, ad, bd, idesc, (dy | cb) ? 1u : 0u);
+                    }
+                umma_commit(&empty[s]);
+                umma_commit(&accf[acc]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue ----------------
+        const int quad = warp & 3, ch = (warp - 2) >> 2;
+        const int p = quad * 32 + lane;                       // pixel within the tile
+        const int yl = p / W, x = p - yl * W;
+        for (int t = 0; t < my_tiles; ++t) {
+            const int acc = t & 1;
+            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * 128 + ch * 16;
+            uint32_t d0[16], d1[16], d2[16];
+            tmem_ld16(taddr, d0);
+            tmem_ld16(taddr + 32, d1);
+            tmem_ld16(taddr + 64, d2);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[acc]);
+            int32_t* xq = xb + ((acc * 2 + ch) * 4) * 32;     // [quad][2][16]
+            if (lane == 31)
+#pragma unroll
+                for (int o = 0; o < 16; ++o) xq[quad * 32 + o] = static_cast<int32_t>(d0[o]);
+            if (lane == 0)
+#pragma unroll
+                for (int o = 0; o < 16; ++o) xq[quad * 32 + 16 + o] = static_cast<int32_t>(d2[o]);
+            // the four warps of this channel half hand their edge columns over (bounded wait)
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[acc * 2 + ch]);
+            if (!mbar_wait(&xbar[acc * 2 + ch], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            const int tile = blockIdx.x + t * gridDim.x;
+            const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
+            const bool valid = yl < Rt && y0 + yl < H;
+            const bool has_l = x > 0, has_r = x < W - 1;
+            uint32_t wd[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int o = j * 4 + k;
+                    int32_t l = __shfl_up_sync(0xffffffffu, static_cast<int32_t>(d0[o]), 1);
+                    int32_t r = __shfl_down_sync(0xffffffffu, static_cast<int32_t>(d2[o]), 1);
+                    if (lane == 0) l = quad > 0 ? xq[(quad - 1) * 32 + o] : 0;
+                    if (lane == 31) r = quad < 3 ? xq[(quad + 1) * 32 + 16 + o] : 0;
+                    const int32_t accv = static_cast<int32_t>(d1[o]) + (has_l ? l : 0) + (has_r ? r : 0);
+                    word |= q_s8(__int2float_rn(accv) * sSc[ch * 16 + o]) << (8 * k);
+                }
+                wd[j] = word;
+            }
+            if (valid) {
+                int8_t* dst = a.out + ((static_cast<size_t>(n) * H + y0 + yl) * W + x) * 32 + ch * 16;
+                *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_free(tmem, 256);
+    }
+}
+
+// 5-D map over the bottleneck planes [8][N][H][W][16] (bytes): box {16, W, Rt + 2, 1, 8}.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static cudaError_t make_bott_map(CUtensorMap* map, const void* base, int N, int H, int W, int Rt) {
+    static EncodeTiledFn encode = nullptr;
+    if (encode == nullptr) {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                         cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) return cudaErrorNotSupported;
+        encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    const cuuint64_t rows = static_cast<cuuint64_t>(N) * H * W;
+    cuuint64_t dims[5] = {16, static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(N), 8};
+    cuuint64_t strides[4] = {16, static_cast<cuuint64_t>(W) * 16, static_cast<cuuint64_t>(H) * W * 16, rows * 16};
+    cuuint32_t box[5] = {16, static_cast<cuuint32_t>(W), static_cast<cuuint32_t>(Rt + 2), 1, 8};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t prepare_conv2(Conv2Plan* plan, const dn8_conv2_args& a) {
+    if (a.W < 1 || a.W > 128 || a.H < 1 || a.N < 1) return cudaErrorInvalidValue;
+    plan->Rt = c2_rows_per_tile(a.H, a.W);
+    plan->stage_bytes = static_cast<uint32_t>(c2_stage_bytes(plan->Rt, a.W));
+    plan->smem = conv2_smem_bytes(a.H, a.W);
+    if (plan->smem > 227 * 1024) return cudaErrorInvalidValue;
+    return make_bott_map(&plan->map, a.x, a.N, a.H, a.W, plan->Rt);
+}
+
+cudaError_t launch_conv2(const Conv2Plan& plan, const dn8_conv2_args& a, int sms, cudaStream_t st) {
+    const int tpi = (a.H + plan.Rt - 1) / plan.Rt;
+    const int ntiles = a.N * tpi;
+    const int grid = ntiles < sms ? ntiles : sms;
+    if (grid <= 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(conv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(plan.smem));
+    if (e != cudaSuccess) return e;
+    conv2_kernel<<<grid, C2_THREADS, plan.smem, st>>>(plan.map, a, plan.Rt, plan.stage_bytes);
+    return cudaGetLastError();
+}
+
+}  // namespace dn8

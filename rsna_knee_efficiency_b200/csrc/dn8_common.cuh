@@ -1,0 +1,197 @@
+// dn8_common.cuh -- device helpers shared by the sm_100a kernels of the INT8 DenseNet169 encoder:
+// mbarriers with bounded waits, bulk / tensor copies, tcgen05 (TMEM allocation, kind::i8 MMA,
+// commit, TMEM loads, fences), UMMA descriptors and the bit-exact prologue arithmetic.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#define DN8_DEV __device__ __forceinline__
+
+namespace dn8 {
+
+// ---- error reporting ------------------------------------------------------------------------
+// Every wait is bounded. A wait that gives up writes its code into the launch's error word (the
+// first code wins) and raises the CTA's abort flag, after which every role leaves its loop; the
+// kernel still frees its TMEM and returns, so the context stays usable.
+enum : int {
+    ERR_NONE = 0,
+    ERR_WAIT_FULL = 1,      // a consumer waited too long for a filled stage
+    ERR_WAIT_EMPTY = 2,     // a producer waited too long for a free stage
+    ERR_WAIT_ACC = 3,       // MMA / epilogue accumulator hand-off
+    ERR_SHAPE = 4,          // launch arguments outside what the kernel supports
+};
+// ~2^32 SM cycles (about 2 s at 2 GHz): far beyond any legitimate wait of these kernels.
+constexpr long long WAIT_LIMIT = 1ll << 32;
+
+DN8_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+DN8_DEV void raise_error(int* err, volatile int* abort_flag, int code) {
+    if (err) atomicCAS(err, 0, code);
+    *abort_flag = 1;
+}
+
+// ---- mbarrier -------------------------------------------------------------------------------
+DN8_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+DN8_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+DN8_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+DN8_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+DN8_DEV bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Waits for the phase of parity `parity` to complete. Returns false (error raised) on timeout or
+// when another role has already aborted.
+DN8_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code) {
+    if (mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > WAIT_LIMIT) {
+            raise_error(err, abort_flag, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---- bulk copies / TMA ----------------------------------------------------------------------
+DN8_DEV void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// 5-D tiled tensor load (no multicast) into CTA shared memory, completing on `bar`.
+DN8_DEV void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                         int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+          "r"(smem_u32(bar))
+        : "memory");
+}
+DN8_DEV void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+// Generic-proxy shared-memory writes made visible to the async proxy (tensor core, TMA).
+DN8_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- tcgen05 --------------------------------------------------------------------------------
+// One full warp allocates; the base address is written to shared memory.
+DN8_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+DN8_DEV void tmem_free(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
+}
+DN8_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+DN8_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 "version 1"): start, leading / stride byte offsets.
+enum : uint32_t { LAYOUT_NONE = 0, LAYOUT_SW32 = 6 };
+DN8_DEV uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
+           (static_cast<uint64_t>(layout) << 61);
+}
+// Instruction descriptor of tcgen05.mma kind::i8: D s32, A u8, B s8, both K-major.
+constexpr uint32_t idesc_u8s8(int M, int N) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+DN8_DEV void umma_u8s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrives once on `bar` when every tcgen05 operation issued so far by this thread has completed.
+DN8_DEV void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+DN8_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+#define DN8_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \
+                  "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+// 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets row (lane base + t).
+DN8_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : DN8_R8(0), DN8_R8(8), DN8_R8(16), DN8_R8(24)
+                 : "r"(taddr) : "memory");
+}
+DN8_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : DN8_R8(0), DN8_R8(8)
+                 : "r"(taddr) : "memory");
+}
+#undef DN8_R8
+
+// ---- named barriers among a subset of warps -------------------------------------------------
+DN8_DEV void named_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- bit-exact prologue / epilogue arithmetic -----------------------------------------------
+// fp16 prologue of 4 store bytes (channels c..c+3, c even): u = rint(255 * sat_f16(A q + B)), the
+// arithmetic of the reference's `pro4h` (src/knee/dense8s_kernels.cu:122-139): q is placed exactly
+// in an fp16 (1024 + (q + 128) - 1152), one fp16 fma with saturation gives v, and a second fp16
+// fma v * 255 + 1024 rounds 255 v to the nearest integer (ties to even) in the low byte.
+// a01 / b01: (A, B) of channels c, c+1 as half2; a23 / b23 of c+2, c+3.
+DN8_DEV uint32_t prologue_f16x4(uint32_t q4, uint32_t a01, uint32_t b01, uint32_t a23, uint32_t b23) {
+    const uint32_t w = q4 ^ 0x80808080u;                 // signed byte q -> unsigned q + 128
+    uint32_t lo = __byte_perm(w, 0x64646464u, 0x4140);   // fp16 pair 1024 + (q + 128)
+    uint32_t hi = __byte_perm(w, 0x64646464u, 0x4342);
+    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(lo) : "r"(0xE480E480u));   // - 1152: exact q
+    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(hi) : "r"(0xE480E480u));
+    asm("fma.rn.sat.f16x2 %0, %0, %1, %2;" : "+r"(lo) : "r"(a01), "r"(b01));
+    asm("fma.rn.sat.f16x2 %0, %0, %1, %2;" : "+r"(hi) : "r"(a23), "r"(b23));
+    asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(lo) : "r"(0x5BF85BF8u), "r"(0x64006400u));  // *255 +1024
+    asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(hi) : "r"(0x5BF85BF8u), "r"(0x64006400u));
+    return __byte_perm(lo, hi, 0x6420);
+}
+
+// fp32 prologue of one store byte `q` (the reference's `pro16`, :99-120): v = sat(fmaf(a, q, b)),
+// u = rint(255 v) as the low byte of fmaf(v, 255, 2^23).
+DN8_DEV uint32_t prologue_f32(int q, float a, float b) {
+    const float f = __int_as_float(0x4B000000 | ((q + 128) & 0xFF)) - 8388736.0f;  // exact q
+    const float v = __saturatef(fmaf(a, f, b));
+    return __float_as_uint(fmaf(v, 255.0f, 8388608.0f)) & 0xFFu;
+}
+DN8_DEV uint32_t prologue_f32x4(uint32_t q4, const float2* ab) {
+    uint32_t r = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int q = static_cast<int>(static_cast<int8_t>((q4 >> (8 * k)) & 0xFF));
+        r |= prologue_f32(q, ab[k].x, ab[k].y) << (8 * k);
+    }
+    return r;
+}
+
+// conv1 epilogue (u8 bottleneck): rint(255 sat(fmaf(g, acc, d))) (reference :598-611).
+DN8_DEV uint32_t epi_u8(int32_t acc, float g, float d) {
+    const float v = __saturatef(fmaf(g, __int2float_rn(acc), d));
+    return __float_as_uint(fmaf(v, 255.0f, 8388608.0f)) & 0xFFu;
+}
+// Symmetric int8 requantisation rint(clamp(t, -127, 127)) as a byte (t + 1.5 * 2^23).
+DN8_DEV uint32_t q_s8(float t) {
+    return __float_as_uint(fminf(fmaxf(t, -127.0f), 127.0f) + 12582912.0f) & 0xFFu;
+}
+
+}  // namespace dn8

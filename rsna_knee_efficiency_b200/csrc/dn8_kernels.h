@@ -1,0 +1,23 @@
+// dn8_kernels.h -- internal launch interface between the C ABI (abi.cu) and the kernels.
+#pragma once
+#include <cstddef>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "../../include/dn8.h"
+
+namespace dn8 {
+
+size_t conv1_smem_bytes(int G);
+cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st);
+
+struct Conv2Plan {
+    CUtensorMap map;      // bottleneck planes, built once per geometry and buffer
+    int Rt;               // image rows per tile
+    uint32_t stage_bytes;
+    size_t smem;
+};
+size_t conv2_smem_bytes(int H, int W);
+cudaError_t prepare_conv2(Conv2Plan* plan, const dn8_conv2_args& a);
+cudaError_t launch_conv2(const Conv2Plan& plan, const dn8_conv2_args& a, int sms, cudaStream_t st);
+
+}  // namespace dn8

@@ -1,0 +1,55 @@
+"""Shared helpers of the tests: seeded plans / tables, random stores in the reference's layouts."""
+from __future__ import annotations
+
+import functools
+
+import numpy as np
+import torch
+
+from rsna_knee_efficiency_b200 import densenet, quant, synth
+
+
+@functools.lru_cache(maxsize=4)
+def plan_tables(img: int, seed: int = 42):
+    """(model, plan, par) for a seeded random DenseNet169 calibrated on synthetic batches."""
+    torch.manual_seed(0)
+    m = densenet.random_init(densenet.DenseNet169(), seed)
+    batches = [torch.from_numpy(b) for b in synth.calibration_batches(2, 2, img, seed=1000 + seed)]
+    cal = quant.calibrate(m, batches)
+    plan = quant.make_plan(m, cal, img)
+    return m, plan, quant.kernel_params(plan)
+
+
+def rand_store(rng: np.random.Generator, shape, kind: str = "uniform") -> np.ndarray:
+    """int8 store bytes: 'uniform' = randint(-127, 128) (the reference's unit tests,
+    kaggle/int8_pack/pack_dense8s.py:233-243); 'relu' = half zeros, the rest |N(0, 40)| clipped to
+    127 (a requantised ReLU distribution)."""
+    if kind == "uniform":
+        return rng.integers(-127, 128, size=shape, dtype=np.int64).astype(np.int8)
+    v = np.minimum(np.abs(rng.normal(0, 40, size=shape)), 127).round()
+    v[rng.random(size=shape) < 0.5] = 0
+    return v.astype(np.int8)
+
+
+def split_store(X: np.ndarray, c0: int):
+    """Channel-last store X [N, HW, c] -> (in0 [N, G0, HW, 32], seg [L, N, HW, 32])."""
+    N, HW, c = X.shape
+    in0 = X[..., :c0].reshape(N, HW, c0 // 32, 32).transpose(0, 2, 1, 3)
+    L = (c - c0) // 32
+    seg = X[..., c0:].reshape(N, HW, L, 32).transpose(2, 0, 1, 3)
+    return np.ascontiguousarray(in0), np.ascontiguousarray(seg)
+
+
+def planes_to_pixels(out: torch.Tensor, rows: int) -> np.ndarray:
+    """Bottleneck planes [8, rows, 16] -> [rows, 128]."""
+    return out.view(8, rows, 16).permute(1, 0, 2).reshape(rows, 128).cpu().numpy()
+
+
+def pixels_to_planes(v: np.ndarray) -> np.ndarray:
+    """[rows, 128] -> [8, rows, 16]."""
+    rows = v.shape[0]
+    return np.ascontiguousarray(v.reshape(rows, 8, 16).transpose(1, 0, 2))
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()

@@ -1,0 +1,87 @@
+"""GPU parity of the per-layer kernels against the CPU oracle (KERNEL arithmetic = the
+reference CUDA kernels'): every byte must match. Random stores as the reference's own unit tests
+(`unit_conv1` / `unit_conv2`, kaggle/int8_pack/pack_dense8s.py:247-320); the output buffers are
+pre-filled with a sentinel so a missed write shows."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from rsna_knee_efficiency_b200 import ops
+from tests.helpers import dev, pixels_to_planes, planes_to_pixels, plan_tables, rand_store, split_store
+
+pytestmark = pytest.mark.gpu
+
+# (block, layer) checked by the reference (pack_dense8s.py:863-864)
+REF_LAYERS = [(0, 0), (0, 5), (1, 0), (1, 7), (2, 20), (3, 0), (3, 31)]
+
+
+def _conv1_case(par, bi, li, c0, N, HW, f16, kind, seed):
+    rng = np.random.default_rng(seed)
+    cin = c0 + 32 * li
+    X = rand_store(rng, (N, HW, cin), kind)
+    in0, seg = split_store(X, c0)
+    rows = N * HW
+    out = torch.full((8 * rows * 16,), 0xA5, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    segd = dev(seg) if li > 0 else torch.zeros(16, dtype=torch.int8, device="cuda")
+    tab = par[f"L{bi}_{li}_abh"] if f16 else par[f"L{bi}_{li}_ab"]
+    ops.conv1(dev(in0), segd, dev(par[f"L{bi}_{li}_w1"]), dev(tab), dev(par[f"L{bi}_{li}_gdu"]),
+              out, c0 // 32, cin // 32, N, HW, f16, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = planes_to_pixels(out, rows)
+    want = orc.conv1(X.reshape(rows, cin), par[f"L{bi}_{li}_w1"],
+                     ab=None if f16 else par[f"L{bi}_{li}_ab"],
+                     abh=par[f"L{bi}_{li}_abh"] if f16 else None,
+                     gd=par[f"L{bi}_{li}_gdu"], mode=orc.KERNEL)
+    return got, want
+
+
+@pytest.mark.parametrize("bi,li", REF_LAYERS)
+@pytest.mark.parametrize("f16", [True, False])
+def test_conv1_ref_layers_512(bi, li, f16):
+    _, plan, par = plan_tables(512)
+    b = plan.blocks[bi]
+    got, want = _conv1_case(par, bi, li, b.c0, 2, b.h * b.w, f16, "uniform", 100 * bi + li)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("N,HW", [(3, 100), (1, 7), (5, 256), (2, 4)])
+def test_conv1_ragged_rows(N, HW):
+    """Row counts that are not multiples of the 128-row tile and tiles straddling images."""
+    _, plan, par = plan_tables(512)
+    got, want = _conv1_case(par, 1, 3, plan.blocks[1].c0, N, HW, True, "relu", 7 * N + HW)
+    np.testing.assert_array_equal(got, want)
+
+
+def _conv2_case(par, bi, li, N, H, W, seed):
+    rng = np.random.default_rng(seed)
+    V = rng.integers(0, 80, size=(N, H, W, 128), dtype=np.int64).astype(np.uint8)
+    rows = N * H * W
+    out = torch.full((rows * 32,), 0x5A, dtype=torch.int8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.conv2(dev(pixels_to_planes(V.reshape(rows, 128))), dev(par[f"L{bi}_{li}_w2k"]),
+              dev(par[f"L{bi}_{li}_c2u"]), out, N, H, W, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = out.view(N, H, W, 32).cpu().numpy()
+    want = orc.conv2(V, par[f"L{bi}_{li}_w2k"], par[f"L{bi}_{li}_c2u"], orc.KERNEL)
+    return got, want
+
+
+@pytest.mark.parametrize("bi,li", [(0, 0), (1, 7), (2, 20), (3, 31)])
+def test_conv2_ref_layers_512(bi, li):
+    _, plan, par = plan_tables(512)
+    b = plan.blocks[bi]
+    got, want = _conv2_case(par, bi, li, 2, b.h, b.w, 7 + 100 * bi + li)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("N,H,W", [(1, 16, 16), (3, 8, 8), (2, 2, 2), (1, 5, 72), (2, 9, 9), (1, 3, 128)])
+def test_conv2_small_and_ragged(N, H, W):
+    _, _, par = plan_tables(512)
+    got, want = _conv2_case(par, 1, 2, N, H, W, N * 1000 + H * 10 + W)
+    np.testing.assert_array_equal(got, want)
