@@ -43,12 +43,14 @@ typedef void* dn8_stream; /* a cudaStream_t; NULL = legacy default stream */
 /* conv1 of dense layer (b, l): replaces `conv1_w64_pl(KArg)` / `conv1_u*(KArg)` (reference
  * src/knee/dense8s_kernels.cu:479-627, launched by `Dense8SEncoder._c1_item` src/knee/dense8s.py:1205-1240).
  * u = prologue(q) per channel, acc = sum_c W[o,c] u_c (int32), out = rint(255 sat(g_o acc + d_o)).
- * Store: in0 [N][G0][HW][32] int8, seg [L][N][HW][32] int8 (groups G0.. read from seg).
+ * Store: in0 [G0][N][HW][32] int8 (group-major: unlike the reference's [N][G0][HW][32], every
+ * 32-channel group of a 128-pixel tile is one contiguous 4 KB run), seg [L][N][HW][32] int8
+ * (groups G0.. read from seg).
  * Output: the u8 bottleneck as 8 planes of 16 channels, [8][N*HW][16]. */
 typedef struct dn8_conv1_args {
     const int8_t* in0;
     const int8_t* seg;
-    const int8_t* w;    /* L*_w1: [G][128][32] int8 */
+    const int8_t* w;    /* L*_w1 [G][128][32] after dn8_prepare_conv1_weights (G * 4096 bytes) */
     const void* ab;     /* prologue table: L*_abh [G*16][4] fp16 (prologue_f16 = 1) or L*_ab [G*32][2] float */
     const float* gd;    /* L*_gdu: [128][2] float */
     uint8_t* out;       /* [8][N*HW][16] */
@@ -64,13 +66,39 @@ int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream);
  * Requires W <= 128. */
 typedef struct dn8_conv2_args {
     const uint8_t* x;   /* bottleneck planes [8][N*H*W][16] */
-    const int8_t* w;    /* L*_w2k: [4][9][32][32] int8 (channel block, tap, out, in) */
+    const int8_t* w;    /* L*_w2k [4][9][32][32] after dn8_prepare_conv2_weights (36864 bytes) */
     const float* sc;    /* L*_c2u: [32] float */
     int8_t* out;        /* store slot [N][H*W][32] */
     int32_t* err;
     int32_t N, H, W;
 } dn8_conv2_args;
 int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream);
+
+/* transition of block b: replaces `trans_w0` / `trans_w1(KArg)` (reference :3077-3268) and the
+ * integer form `trans_q128(KArg)` (:176-422, MODE 1), launched by `_trans_item`
+ * (src/knee/dense8s.py:1242-1272). Prologue as conv1 on all G = c_tot / 32 groups, 1x1 conv
+ * c_tot -> c_tot / 2, the four accumulators of every 2x2 square summed exactly (int32), then
+ * q = rint(clamp(k_o * s, +-127)), k = T*_gd[o][0], into the next block's group-major in0
+ * [c_tot/64][N][H*W/4][32]. H and W even. */
+typedef struct dn8_trans_args {
+    const int8_t* in0;
+    const int8_t* seg;
+    const int8_t* w;    /* T*_w [G][c_out][32] after dn8_prepare_trans_weights (G * c_out * 32 bytes) */
+    const void* ab;     /* T*_abh (prologue_f16 = 1) or T*_ab */
+    const float* gd;    /* T*_gd: [c_out][2] float */
+    int8_t* out;        /* next block's in0 */
+    int32_t* err;
+    int32_t G0, G, N, H, W;
+    int32_t prologue_f16;
+} dn8_trans_args;
+int dn8_trans(const dn8_trans_args* a, dn8_stream stream);
+
+/* ---- weight preparation (host memory to host memory, once per pack) ------------------------
+ * The kernels read their weights with bulk copies straight into the tensor cores' shared-memory
+ * operand layout; these functions permute the reference pack tables into that layout. */
+int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out);               /* G*4096 B */
+int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out); /* G*cout*32 B */
+int dn8_prepare_conv2_weights(const int8_t* w2k, uint8_t* out);                         /* 36864 B */
 
 const char* dn8_last_error(void);   /* message of the calling thread's last failed call */
 int dn8_device_sms(int device);     /* SM count used to size persistent grids (0 on error) */

@@ -21,9 +21,18 @@ class Conv2Args(ctypes.Structure):
                 ("N", I32), ("H", I32), ("W", I32)]
 
 
+class TransArgs(ctypes.Structure):
+    _fields_ = [("in0", P), ("seg", P), ("w", P), ("ab", P), ("gd", P), ("out", P), ("err", P),
+                ("G0", I32), ("G", I32), ("N", I32), ("H", I32), ("W", I32), ("prologue_f16", I32)]
+
+
 EXPORTS = {
     "dn8_conv1": ([ctypes.POINTER(Conv1Args), P], ctypes.c_int),
     "dn8_conv2": ([ctypes.POINTER(Conv2Args), P], ctypes.c_int),
+    "dn8_trans": ([ctypes.POINTER(TransArgs), P], ctypes.c_int),
+    "dn8_prepare_conv1_weights": ([P, I32, P], ctypes.c_int),
+    "dn8_prepare_trans_weights": ([P, I32, I32, P], ctypes.c_int),
+    "dn8_prepare_conv2_weights": ([P, P], ctypes.c_int),
     "dn8_last_error": ([], ctypes.c_char_p),
     "dn8_device_sms": ([ctypes.c_int], ctypes.c_int),
 }

@@ -89,4 +89,59 @@ int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream) {
     return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_conv2 launch");
 }
 
+int dn8_trans(const dn8_trans_args* a, dn8_stream stream) {
+    if (a == nullptr) return fail(DN8_EINVAL, "dn8_trans: null arguments");
+    if (a->G < 2 || a->G % 2 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->H < 2 || a->W < 2 || a->H % 2 ||
+        a->W % 2)
+        return fail(DN8_EINVAL, "dn8_trans: bad geometry G0=%d G=%d N=%d H=%d W=%d", a->G0, a->G, a->N, a->H, a->W);
+    if (a->G * 16 > 640) return fail(DN8_EINVAL, "dn8_trans: c_out %d > 640", a->G * 16);
+    if (!aligned16(a->in0) || !aligned16(a->seg) || !aligned16(a->w) || !aligned16(a->ab) ||
+        !aligned16(a->out) || a->gd == nullptr)
+        return fail(DN8_EINVAL, "dn8_trans: pointers must be non-null and 16-byte aligned");
+    int sms = 0;
+    if (int s = current_sms(&sms)) return s;
+    cudaError_t e = dn8::launch_trans(*a, sms, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_trans launch");
+}
+
+// [rows][32] tile -> tcgen05 K-major 32-byte-swizzle layout: 16-byte half h of row r goes to
+// r * 32 + ((h ^ ((r >> 2) & 1)) << 4).
+static void swizzle32_tile(const int8_t* src, int rows, uint8_t* dst) {
+    for (int r = 0; r < rows; ++r)
+        for (int h = 0; h < 2; ++h)
+            std::memcpy(dst + r * 32 + ((h ^ ((r >> 2) & 1)) << 4), src + r * 32 + h * 16, 16);
+}
+
+int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out) {
+    if (w1 == nullptr || out == nullptr || G < 1) return fail(DN8_EINVAL, "dn8_prepare_conv1_weights: bad arguments");
+    for (int g = 0; g < G; ++g) swizzle32_tile(w1 + static_cast<size_t>(g) * 4096, 128, out + static_cast<size_t>(g) * 4096);
+    return DN8_OK;
+}
+
+int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out) {
+    if (tw == nullptr || out == nullptr || G < 1 || cout < 32 || cout % 32)
+        return fail(DN8_EINVAL, "dn8_prepare_trans_weights: bad arguments");
+    const int nc = dn8::trans_chunk(cout), nchunks = cout / nc;
+    // [nchunks][G][nc rows][32]: chunk c holds output channels c * nc .. c * nc + nc - 1
+    for (int c = 0; c < nchunks; ++c)
+        for (int g = 0; g < G; ++g)
+            swizzle32_tile(tw + (static_cast<size_t>(g) * cout + static_cast<size_t>(c) * nc) * 32, nc,
+                           out + (static_cast<size_t>(c) * G + g) * nc * 32);
+    return DN8_OK;
+}
+
+int dn8_prepare_conv2_weights(const int8_t* w2k, uint8_t* out) {
+    if (w2k == nullptr || out == nullptr) return fail(DN8_EINVAL, "dn8_prepare_conv2_weights: bad arguments");
+    // w2k [cblk][tap][o][32] -> [dy][cblk][half][dx * 32 + o][16] (tap = 3 dy + dx)
+    for (int blk = 0; blk < 4; ++blk)
+        for (int tap = 0; tap < 9; ++tap)
+            for (int o = 0; o < 32; ++o)
+                for (int h = 0; h < 2; ++h) {
+                    const int dy = tap / 3, dx = tap % 3;
+                    std::memcpy(out + ((dy * 4 + blk) * 2 + h) * 1536 + (dx * 32 + o) * 16,
+                                w2k + ((blk * 9 + tap) * 32 + o) * 32 + h * 16, 16);
+                }
+    return DN8_OK;
+}
+
 }  // extern "C"

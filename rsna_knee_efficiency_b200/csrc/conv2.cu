@@ -9,8 +9,9 @@
 //     D[p][dx, o] = sum_{dy, c} W[dy, dx][o][c] * X[y(p) + dy - 1, x(p)][c].
 // The epilogue adds the three column taps: out[p][o] = D[p-1][0, o] + D[p][1, o] + D[p+1][2, o]
 // (neighbours through warp shuffles, zero outside the row), so no column halo is ever loaded.
-// One 5-D TMA load per tile brings the 8 bottleneck planes x (Rt + 2) rows; rows outside the
-// image arrive zero-filled (the convolution's zero padding).
+// One 4-D TMA load per tile brings the 8 bottleneck planes x (Rt + 2) image rows; rows outside
+// the image arrive zero-filled (the convolution's zero padding). The weights arrive prepared
+// (dn8_prepare_conv2_weights) in one bulk copy and stay resident.
 // Warp roles: warp 0 TMEM owner + TMA producer, warp 1 MMA issuer, warps 2-9 epilogue (warp w
 // reads TMEM lanes 32*(w%4).. and 16 of the 32 outputs).
 #include "dn8_common.cuh"
@@ -37,7 +38,7 @@ static inline size_t c2_stage_bytes(int Rt, int W) {
 size_t conv2_smem_bytes(int H, int W) {
     const int Rt = c2_rows_per_tile(H, W);
     return 1024 + C2_W_BYTES + C2_STAGES * c2_stage_bytes(Rt, W) + 128 + 2 * 2 * 4 * 2 * 16 * 4 +
-           8 * (2 * C2_STAGES + 8) + 16;
+           8 * (2 * C2_STAGES + 9) + 16;
 }
 
 __global__ void __launch_bounds__(C2_THREADS, 1)
@@ -53,7 +54,8 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
     uint64_t* accf = empty + C2_STAGES;
     uint64_t* acce = accf + 2;
     uint64_t* xbar = acce + 2;                             // [2 acc][2 ch]: neighbour exchange
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(xbar + 4);
+    uint64_t* wfull = xbar + 4;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(wfull + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -73,35 +75,37 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             mbar_init(&acce[k], 8);
         }
         for (int k = 0; k < 4; ++k) mbar_init(&xbar[k], 4);
+        mbar_init(&wfull[0], 1);
         *s_abort = 0;
         mbar_fence_init();
         prefetch_tensormap(&tmap);
     }
-    // weights: w2k [cblk][tap][o][32] -> [dy][cblk][half][dx * 32 + o][16]
-    for (int q = threadIdx.x; q < C2_W_BYTES / 16; q += C2_THREADS) {
-        const int hh = q & 1, o = (q >> 1) & 31, tap = (q >> 6) % 9, blk = (q >> 6) / 9;
-        const int dy = tap / 3, dx = tap % 3;
-        *reinterpret_cast<uint4*>(sW + ((dy * 4 + blk) * 2 + hh) * 1536 + (dx * 32 + o) * 16) =
-            __ldg(reinterpret_cast<const uint4*>(a.w) + q);
+    // exact int32 -> float through the magic add when every channel saturates at +-2^22 (see gemm.cu)
+    int ok = 1;
+    if (threadIdx.x < 32) {
+        const float sc = a.sc[threadIdx.x];
+        sSc[threadIdx.x] = sc;
+        ok = sc * 4194304.0f >= 127.0f ? 1 : 0;
     }
-    if (threadIdx.x < 32) sSc[threadIdx.x] = a.sc[threadIdx.x];
-    fence_async_smem();
     if (warp == 0) tmem_alloc(s_tmem, 256);
     tc_fence_before();
-    __syncthreads();
+    const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
+        if (lane == 0 && my_tiles > 0) {
+            // the prepared weights [dy][cblk][half][dx * 32 + o][16] in one bulk copy
+            mbar_expect_tx(&wfull[0], C2_W_BYTES);
+            bulk_g2s(sW, a.w, C2_W_BYTES, &wfull[0]);
             for (int t = 0; t < my_tiles; ++t) {
                 const int s = t % C2_STAGES;
                 if (!mbar_wait(&empty[s], ((t / C2_STAGES) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
                 const int tile = blockIdx.x + t * gridDim.x;
                 const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
                 mbar_expect_tx(&full[s], 8u * PL);
-                tma_load_5d(sX + s * stage_bytes, &tmap, &full[s], 0, 0, y0 - 1, n, 0);
+                tma_load_4d(sX + s * stage_bytes, &tmap, &full[s], 0, y0 - 1, n, 0);
             }
         }
         __syncwarp();
@@ -110,7 +114,8 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         if (lane == 0) {
             const uint32_t idesc = idesc_u8s8(128, 96);
             const uint32_t x0 = smem_u32(sX), w0 = smem_u32(sW);
-            for (int t = 0; t < my_tiles; ++t) {
+            const bool wok = my_tiles == 0 || mbar_wait(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+            for (int t = 0; t < my_tiles && wok; ++t) {
                 const int acc = t & 1, s = t % C2_STAGES;
                 if (!mbar_wait(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
                 tc_fence_after();
@@ -175,7 +180,9 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
                     if (lane == 0) l = quad > 0 ? xq[(quad - 1) * 32 + o] : 0;
                     if (lane == 31) r = quad < 3 ? xq[(quad + 1) * 32 + 16 + o] : 0;
                     const int32_t accv = static_cast<int32_t>(d1[o]) + (has_l ? l : 0) + (has_r ? r : 0);
-                    word |= q_s8(__int2float_rn(accv) * sSc[ch * 16 + o]) << (8 * k);
+                    const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
+                                             : __int2float_rn(accv);
+                    word |= q_s8(f * sSc[ch * 16 + o]) << (8 * k);
                 }
                 wd[j] = word;
             }
@@ -194,7 +201,9 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
     }
 }
 
-// 5-D map over the bottleneck planes [8][N][H][W][16] (bytes): box {16, W, Rt + 2, 1, 8}.
+// 4-D map over the bottleneck planes [8][N][H][W * 16 bytes] with 8-byte elements, so that a box
+// row is a whole image row (16 W bytes; TMA moves long rows far faster than 16-byte ones):
+// box {2W, Rt + 2, 1, 8}; rows outside [0, H) are zero-filled.
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -210,11 +219,11 @@ static cudaError_t make_bott_map(CUtensorMap* map, const void* base, int N, int 
         encode = reinterpret_cast<EncodeTiledFn>(fn);
     }
     const cuuint64_t rows = static_cast<cuuint64_t>(N) * H * W;
-    cuuint64_t dims[5] = {16, static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(N), 8};
-    cuuint64_t strides[4] = {16, static_cast<cuuint64_t>(W) * 16, static_cast<cuuint64_t>(H) * W * 16, rows * 16};
-    cuuint32_t box[5] = {16, static_cast<cuuint32_t>(W), static_cast<cuuint32_t>(Rt + 2), 1, 8};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<void*>(base), dims, strides, box, estr,
+    cuuint64_t dims[4] = {2 * static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(N), 8};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(W) * 16, static_cast<cuuint64_t>(H) * W * 16, rows * 16};
+    cuuint32_t box[4] = {2 * static_cast<cuuint32_t>(W), static_cast<cuuint32_t>(Rt + 2), 1, 8};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;

@@ -67,17 +67,20 @@ DN8_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* a
 }
 
 // ---- bulk copies / TMA ----------------------------------------------------------------------
+// Contiguous global -> shared copy (16-byte aligned, size a multiple of 16), completing on `bar`.
+DN8_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
 DN8_DEV void prefetch_l2_bulk(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
-// 5-D tiled tensor load (no multicast) into CTA shared memory, completing on `bar`.
-DN8_DEV void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
-                         int c3, int c4) {
+// 4-D tiled tensor load (no multicast) into CTA shared memory, completing on `bar`.
+DN8_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
     asm volatile(
-        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
-          "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
         : "memory");
 }
 DN8_DEV void prefetch_tensormap(const CUtensorMap* map) {
@@ -141,7 +144,49 @@ DN8_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
                  : DN8_R8(0), DN8_R8(8)
                  : "r"(taddr) : "memory");
 }
+DN8_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+                 "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+                   "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+                   "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+                   "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+                   "r"(r[29]), "r"(r[30]), "r"(r[31])
+                 : "memory");
+}
+DN8_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 #undef DN8_R8
+
+// Accumulators start at ACC_MAGIC (the bits of the float 1.5 * 2^23): MAGIC + acc read as a float is
+// 1.5 * 2^23 + acc exactly while |acc| < 2^22, so (float)acc is one subtraction.
+constexpr uint32_t ACC_MAGIC = 0x4B400000u;
+constexpr float ACC_MAGIC_F = 12582912.0f;
+
+// ---- packed fp32 pairs (sm_100 f32x2) --------------------------------------------------------
+DN8_DEV unsigned long long f2_pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+DN8_DEV void f2_unpack(unsigned long long r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+DN8_DEV unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+DN8_DEV unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+DN8_DEV unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 
 // ---- named barriers among a subset of warps -------------------------------------------------
 DN8_DEV void named_sync(int id, int nthreads) {

@@ -7,8 +7,9 @@
 
 namespace dn8 {
 
-size_t conv1_smem_bytes(int G);
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st);
+cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st);
+int trans_chunk(int cout);
 
 struct Conv2Plan {
     CUtensorMap map;      // bottleneck planes, built once per geometry and buffer

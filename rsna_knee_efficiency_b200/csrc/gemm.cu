@@ -1,0 +1,505 @@
+// gemm.cu -- the "prologue GEMM" kernels of the encoder on sm_100a: conv1 of every dense layer and
+// the transitions. Both read a block store whose 32-channel groups are all group-major,
+// [G][N][HW][32] int8 (block input groups first, then the layer segments), apply the consumer's
+// BatchNorm + ReLU + u8 quantisation (the prologue), multiply on tcgen05 (kind::i8,
+// u8 x s8 -> s32 in TMEM) and requantise in the epilogue.
+//
+//   conv1      : M = N*HW pixels, N = 128, K = c_in; out = rint(255 sat(g acc + d)) as the u8
+//                bottleneck planes [8][M][16] (reference conv1w_body, dense8s_kernels.cu:479-627).
+//   transition : M = N*HW/4 pooled pixels, N = c_out (chunks of 128 or 256), K = c_tot. For every
+//                K group the four pixels of each 2x2 square are four A sub-tiles multiplied by the
+//                same weights into ONE accumulator: s = the sum of the four 1x1 outputs, exact in
+//                int32 (the integer form gemm_q MODE 1, :375-389); q = rint(clamp(k s, +-127)) into
+//                the next block's group-major input [c_out/32][N][HW/4][32].
+//
+// Pipeline stage = 4 "units" of 128 rows x 32 bytes (16 KB of A, 4 MMAs M128 x NC x K32, one
+// commit): conv1 takes 4 consecutive K groups per stage, the transition the 4 pixels of each
+// square of one K group. Every tcgen05 issue from the single MMA thread costs ~100-200 cycles, so
+// issuing 4 MMAs per wait / commit is what keeps the tensor core fed. The store bytes of a stage
+// arrive by bulk async copies into a shared-memory ring (explicit bytes in flight, no L1 staging).
+// Persistent, one CTA per SM, 19 warps:
+//   warp 0       TMEM owner and MMA issuer (lane 0).
+//   warp 1       store producer (lane 0): bulk copies into the raw ring.
+//   warp 2       weight producer (lane 0): UMMA-ready weight tiles, resident when they fit.
+//   warps 3-10   prologue: one warp per unit, raw ring -> BN/ReLU/u8 -> 32B-swizzled operands.
+//   warps 11-18  epilogue: warp w reads TMEM lanes 32*(w%4).. and half of the NC columns.
+#include "dn8_common.cuh"
+#include "dn8_kernels.h"
+
+namespace dn8 {
+
+constexpr int GM_WARPS = 19;
+constexpr int GM_THREADS = 32 * GM_WARPS;
+constexpr int SMEM_BUDGET = 225 * 1024;
+
+// KSTEP K groups of KSUB sub-tiles per stage (KSTEP * KSUB = 4 units); SR raw slots, SA operand slots
+template <bool TRANS> struct GemmCfg;
+template <> struct GemmCfg<false> {                // conv1
+    static constexpr int KSUB = 1, KSTEP = 4, SR = 4, SA = 4;
+};
+template <> struct GemmCfg<true> {                 // transition
+    static constexpr int KSUB = 4, KSTEP = 1, SR = 4, SA = 4;
+};
+constexpr int UNITS = 4;
+
+struct GemmArgs {
+    const int8_t* in0;        // block input groups [G0][N][HW][32]
+    const int8_t* seg;        // layer segments [L][N][HW][32]
+    const uint8_t* wu;        // UMMA-ready weights [nchunks][G][NC rows x 32 B, 32B-swizzled]
+    const void* ab;           // prologue table (fp16 pairs or fp32 pairs)
+    const float* gd;          // epilogue table [cout][2]
+    void* out;
+    int* err;
+    int G0, G, N, HW, W;      // W: image width (transition)
+    int rows;                 // GEMM rows: N*HW (conv1) or N*HW/4 (transition)
+    int cout, nc, nchunks;    // output channels, channels per chunk, chunks
+    int b_resident;           // 1: all G weight tiles stay in shared memory
+    int sb;                   // weight ring stages when streamed
+    int raw_bytes;            // raw ring slot size (a whole stage)
+};
+
+// Byte range [first, end) of the flattened input pixels (n * HW + y * W + x) a transition tile of
+// pooled pixels [m0, m0 + cnt) reads: whole input rows from 2 * oy(first) to 2 * oy(last) + 1.
+DN8_DEV void trans_span(int m0, int cnt, int HW, int W, int* first, int* end) {
+    const int HW4 = HW >> 2, W2 = W >> 1;
+    const int n0 = m0 / HW4, oy0 = (m0 - n0 * HW4) / W2;
+    const int m1 = m0 + cnt - 1;
+    const int n1 = m1 / HW4, oy1 = (m1 - n1 * HW4) / W2;
+    *first = n0 * HW + 2 * oy0 * W;
+    *end = n1 * HW + (2 * oy1 + 2) * W;
+}
+
+static size_t gemm_layout(bool trans, int G, int nc, int nchunks, int raw_bytes, int* sb, int* resident) {
+    const int sr = trans ? GemmCfg<true>::SR : GemmCfg<false>::SR, sa = trans ? GemmCfg<true>::SA : GemmCfg<false>::SA;
+    const int kstep = trans ? GemmCfg<true>::KSTEP : GemmCfg<false>::KSTEP;
+    const size_t fixed = static_cast<size_t>(sr) * raw_bytes + static_cast<size_t>(sa) * UNITS * 4096;
+    const size_t misc = 1024 + static_cast<size_t>(G) * 256 + static_cast<size_t>(trans ? 640 : 128) * 8 + 8 * 96 + 64;
+    const size_t btile = static_cast<size_t>(nc) * 32;
+    if (nchunks == 1 && fixed + misc + btile * G <= SMEM_BUDGET) {
+        *resident = 1;
+        *sb = G;
+        return fixed + misc + btile * G;
+    }
+    *resident = 0;
+    // streamed: a ring of `s` stages of kstep weight tiles
+    int s = static_cast<int>((SMEM_BUDGET - fixed - misc) / (btile * kstep));
+    s = s > 4 ? 4 : s;
+    *sb = s;
+    return fixed + misc + btile * kstep * s;
+}
+
+template <bool F16, bool TRANS>
+__global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
+    using Cfg = GemmCfg<TRANS>;
+    constexpr int KSUB = Cfg::KSUB, KSTEP = Cfg::KSTEP, SR = Cfg::SR, SA = Cfg::SA;
+    constexpr int ASTAGE = UNITS * 4096;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int NC = a.nc, G = a.G, G0 = a.G0, HW = a.HW, rows = a.rows;
+    const int btile = NC * 32, RB = a.raw_bytes;
+    uint8_t* sR = smem;                                          // [SR][RB] raw store bytes
+    uint8_t* sA = sR + SR * RB;                                  // [SA][KSUB][128][32] swizzled
+    uint8_t* sB = sA + SA * ASTAGE;                              // weights
+    const int bstage = KSTEP * btile;                            // weight bytes of a streamed stage
+    uint8_t* sTab = sB + (a.b_resident ? static_cast<size_t>(G) * btile : static_cast<size_t>(a.sb) * bstage);
+    float2* sGd = reinterpret_cast<float2*>(sTab + G * 256);
+    uint64_t* fullR = reinterpret_cast<uint64_t*>(sGd + (TRANS ? 640 : 128));
+    uint64_t* freeR = fullR + SR;
+    uint64_t* fullA = freeR + SR;
+    uint64_t* emptyA = fullA + SA;
+    uint64_t* fullB = emptyA + SA;                               // [8]
+    uint64_t* emptyB = fullB + 8;
+    uint64_t* accf = emptyB + 8;
+    uint64_t* acce = accf + 2;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acce + 2);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntm = (rows + 127) / 128;
+    const int ntiles = ntm * a.nchunks;
+    const int my_tiles = static_cast<int>(blockIdx.x) < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int NS = (G + KSTEP - 1) / KSTEP;                     // stages per tile
+    const int T = my_tiles * NS;
+    const uint32_t tcols = NC > 128 ? 512u : 256u;
+    const size_t gstride = static_cast<size_t>(a.N) * HW * 32;   // one store group
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SR; ++s) {
+            mbar_init(&fullR[s], 1);
+            mbar_init(&freeR[s], UNITS);
+        }
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(&fullA[s], UNITS);
+            mbar_init(&emptyA[s], 1);
+        }
+        for (int s = 0; s < 8; ++s) {
+            mbar_init(&fullB[s], 1);
+            mbar_init(&emptyB[s], 1);
+        }
+        for (int k = 0; k < 2; ++k) {
+            mbar_init(&accf[k], 1);
+            mbar_init(&acce[k], 8);
+        }
+        *s_abort = 0;
+        mbar_fence_init();
+    }
+    if (F16) {
+        for (int i = threadIdx.x; i < G * 16; i += GM_THREADS)
+            reinterpret_cast<uint2*>(sTab)[i] = reinterpret_cast<const uint2*>(a.ab)[i];
+    } else {
+        for (int i = threadIdx.x; i < G * 32; i += GM_THREADS)
+            reinterpret_cast<float2*>(sTab)[i] = reinterpret_cast<const float2*>(a.ab)[i];
+    }
+    // The epilogue converts int32 -> float with the 1.5 * 2^23 magic add, exact for |acc| < 2^22.
+    // Larger accumulators convert to values of the same sign and magnitude >= 2^22; that is
+    // harmless when every channel already saturates at +-2^22, which is checked here per CTA.
+    int ok = 1;
+    for (int i = threadIdx.x; i < a.cout; i += GM_THREADS) {
+        const float2 p = reinterpret_cast<const float2*>(a.gd)[i];
+        sGd[i] = p;
+        if (TRANS) ok &= (p.x * 4194304.0f >= 127.0f) ? 1 : 0;
+        else ok &= (fmaf(p.x, 4194304.0f, p.y) >= 1.0f && fmaf(p.x, -4194304.0f, p.y) <= 0.0f) ? 1 : 0;
+    }
+    if (warp == 0) tmem_alloc(s_tmem, tcols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+    if (warp >= 11) {                                  // arm both accumulators with MAGIC
+        uint32_t arm[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
+        const int quad = warp & 3, half = (warp - 11) >> 2;
+        for (int acc = 0; acc < 2; ++acc)
+            for (int cb = 0; cb < (NC >> 1); cb += 32)
+                tmem_st32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * (NC >> 1) + cb, arm);
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    const int fast_cvt = __syncthreads_and(ok);
+    tc_fence_after();
+
+    if (warp == 0) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_u8s8(128, NC);
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+            bool ok_run = true;
+            if (a.b_resident && T > 0) ok_run = mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+            int i = 0;
+            for (int t = 0; t < my_tiles && ok_run; ++t) {
+                const int acc = t & 1;
+                if (!mbar_wait(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+                tc_fence_after();
+                for (int j = 0; j < NS; ++j, ++i) {
+                    const int s = i % SA;
+                    const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
+                    if (!mbar_wait(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                    uint32_t bbase;
+                    int sbi = 0;
+                    if (a.b_resident) {
+                        bbase = b0 + j * KSTEP * btile;
+                    } else {
+                        sbi = i % a.sb;
+                        if (!mbar_wait(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                        bbase = b0 + sbi * bstage;
+                    }
+                    tc_fence_after();
+                    const uint32_t abase = a0 + s * ASTAGE;
+#pragma unroll
+                    for (int x = 0; x < UNITS; ++x) {
+                        // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
+                        if (TRANS || x < gc) {
+                            const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
+                            const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
+                            umma_u8s8(tmem + acc * NC, ad, bd, idesc, 1u);   // accumulators start at MAGIC
+                        }
+                    }
+                    umma_commit(&emptyA[s]);
+                    if (!a.b_resident) umma_commit(&emptyB[sbi]);
+                }
+                if (!ok_run) break;
+                umma_commit(&accf[acc]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- store producer ----------------
+        if (lane == 0) {
+            int i = 0;
+            for (int t = 0; t < my_tiles; ++t) {
+                const int tile = blockIdx.x + t * gridDim.x;
+                const int m0 = (tile / a.nchunks) * 128;
+                const int cnt = min(128, rows - m0);
+                size_t off;
+                uint32_t bytes;
+                if (TRANS) {
+                    int first, end;
+                    trans_span(m0, cnt, HW, a.W, &first, &end);
+                    off = static_cast<size_t>(first) * 32;
+                    bytes = static_cast<uint32_t>(end - first) * 32;
+                } else {
+                    off = static_cast<size_t>(m0) * 32;
+                    bytes = static_cast<uint32_t>(cnt) * 32;
+                }
+                bool ok_run = true;
+                for (int j = 0; j < NS; ++j, ++i) {
+                    const int s = i % SR;
+                    const int gc = min(KSTEP, G - j * KSTEP);
+                    if (!mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
+                    mbar_expect_tx(&fullR[s], bytes * gc);
+                    for (int x = 0; x < gc; ++x) {                   // one copy per K group, 4 KB apart
+                        const int g = j * KSTEP + x;
+                        const int8_t* src = g < G0 ? a.in0 + g * gstride + off : a.seg + (g - G0) * gstride + off;
+                        bulk_g2s(sR + s * RB + x * (RB / KSTEP), src, bytes, &fullR[s]);
+                    }
+                }
+                if (!ok_run) break;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // ---------------- weight producer ----------------
+        if (lane == 0 && T > 0) {
+            if (a.b_resident) {
+                mbar_expect_tx(&fullB[0], static_cast<uint32_t>(G * btile));
+                bulk_g2s(sB, a.wu, static_cast<uint32_t>(G * btile), &fullB[0]);
+            } else {
+                int i = 0;
+                for (int t = 0; t < my_tiles; ++t) {
+                    const int tile = blockIdx.x + t * gridDim.x;
+                    const int chunk = tile % a.nchunks;
+                    bool ok_run = true;
+                    for (int j = 0; j < NS; ++j, ++i) {
+                        const int s = i % a.sb;
+                        const int gc = min(KSTEP, G - j * KSTEP);
+                        if (!mbar_wait(&emptyB[s], ((i / a.sb) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
+                        // the gc weight tiles of the stage are contiguous in the prepared table
+                        mbar_expect_tx(&fullB[s], static_cast<uint32_t>(gc * btile));
+                        bulk_g2s(sB + s * bstage, a.wu + (static_cast<size_t>(chunk) * G + j * KSTEP) * btile,
+                                 static_cast<uint32_t>(gc * btile), &fullB[s]);
+                    }
+                    if (!ok_run) break;
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp <= 10) {
+        // ---------------- prologue ----------------
+        // One warp owns a whole unit (128 rows x 32 B = 256 chunks of 16 B; chunk c = jj * 32 + lane is
+        // row c / 2, half c % 2), so every shared-memory access of the warp is 512 contiguous bytes;
+        // the 8 warps work on two stages at once.
+        const int pw = warp - 3;
+        const int h = lane & 1;
+        const int W = a.W, W2 = W >> 1;
+        for (int u = pw; u < T * UNITS; u += 8) {
+            const int i = u / UNITS, x = u - i * UNITS;
+            const int s = i % SR, sa = i % SA;
+            const int t = i / NS, j = i - t * NS;
+            const int gc = min(KSTEP, G - j * KSTEP);
+            const bool active = TRANS || x < gc;                  // conv1: the tile's last stage may be short
+            const int g = TRANS ? j : j * KSTEP + x;              // K group of this unit
+            int off[8];
+            if (TRANS) {
+                // pooled pixel m0 + r -> global pooled row gr (= n * H/2 + oy) and column ox; its input
+                // pixel (2 oy + dy, 2 ox + dx) sits 2W (gr - gr0) + dy W + 2 ox + dx pixels after the
+                // first pixel of the copied span
+                const int tile = blockIdx.x + t * gridDim.x;
+                const int m0 = (tile / a.nchunks) * 128;
+                const int gr0 = m0 / W2;
+                int m = min(m0 + (lane >> 1), rows - 1);
+                int gr = m / W2, ox = m - gr * W2;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    off[jj] = (2 * W * (gr - gr0) + (x >> 1) * W + 2 * ox + (x & 1)) * 32 + h * 16;
+                    if (jj < 7) {                         // next chunk row: +16 pooled pixels
+                        const int step = min(16, rows - 1 - m);
+                        m += step;
+                        ox += step;
+                        while (ox >= W2) { ox -= W2; ++gr; }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) off[jj] = x * 4096 + (jj * 32 + lane) * 16;
+            }
+            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
+            uint4 q[8];
+            if (active) {
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) q[jj] = *reinterpret_cast<const uint4*>(sR + s * RB + off[jj]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&freeR[s]);
+            uint4 res[8];
+            if (active) {
+                if (F16) {
+                    const uint4* tb = reinterpret_cast<const uint4*>(sTab + (g * 16 + h * 8) * 8);
+                    const uint4 t0 = tb[0], t1 = tb[1], t2 = tb[2], t3 = tb[3];    // 8 channel pairs (A, B)
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        res[jj].x = prologue_f16x4(q[jj].x, t0.x, t0.y, t0.z, t0.w);
+                        res[jj].y = prologue_f16x4(q[jj].y, t1.x, t1.y, t1.z, t1.w);
+                        res[jj].z = prologue_f16x4(q[jj].z, t2.x, t2.y, t2.z, t2.w);
+                        res[jj].w = prologue_f16x4(q[jj].w, t3.x, t3.y, t3.z, t3.w);
+                    }
+                } else {
+                    const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32 + h * 16;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        res[jj].x = prologue_f32x4(q[jj].x, tb);
+                        res[jj].y = prologue_f32x4(q[jj].y, tb + 4);
+                        res[jj].z = prologue_f32x4(q[jj].z, tb + 8);
+                        res[jj].w = prologue_f32x4(q[jj].w, tb + 12);
+                    }
+                }
+            }
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+            if (active) {
+                uint8_t* dst = sA + sa * ASTAGE + x * 4096;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const int r = (jj * 32 + lane) >> 1;
+                    *reinterpret_cast<uint4*>(dst + r * 32 + ((h ^ ((r >> 2) & 1)) << 4)) = res[jj];
+                }
+                fence_async_smem();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&fullA[sa]);
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        // TMEM accumulators hold MAGIC + acc (they are re-armed with MAGIC after every read, and
+        // every MMA accumulates), so the int -> float conversion is one packed subtraction.
+        const int quad = warp & 3, half = (warp - 11) >> 2;
+        const int ncol = NC >> 1;                              // columns of this warp
+        const float4* gd4 = reinterpret_cast<const float4*>(sGd);
+        uint32_t arm[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
+        for (int t = 0; t < my_tiles; ++t) {
+            const int acc = t & 1;
+            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            tc_fence_after();
+            const int tile = blockIdx.x + t * gridDim.x;
+            const int chunk = tile % a.nchunks;
+            const int m = (tile / a.nchunks) * 128 + quad * 32 + lane;
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
+            for (int cb = 0; cb < ncol; cb += 32) {
+                uint32_t v[32];
+                tmem_ld32(taddr + cb, v);
+                tmem_wait_ld();
+                tmem_st32(taddr + cb, arm);
+                const int c0 = chunk * NC + half * ncol + cb;      // first output channel
+                uint32_t wd[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t b[4];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int c = 4 * j + 2 * e;
+                        float f0, f1;
+                        if (fast_cvt) {
+                            f2_unpack(f2_add(f2_pack(__uint_as_float(v[c]), __uint_as_float(v[c + 1])),
+                                             f2_pack(-ACC_MAGIC_F, -ACC_MAGIC_F)), f0, f1);
+                        } else {
+                            f0 = __int2float_rn(static_cast<int32_t>(v[c] - ACC_MAGIC));
+                            f1 = __int2float_rn(static_cast<int32_t>(v[c + 1] - ACC_MAGIC));
+                        }
+                        const float4 p = gd4[(c0 + c) >> 1];           // (g, d) of channels c0+c, c0+c+1
+                        float r0, r1;
+                        if (TRANS) {
+                            f2_unpack(f2_mul(f2_pack(p.x, p.z), f2_pack(f0, f1)), r0, r1);
+                            r0 = fminf(fmaxf(r0, -127.0f), 127.0f);
+                            r1 = fminf(fmaxf(r1, -127.0f), 127.0f);
+                            f2_unpack(f2_add(f2_pack(r0, r1), f2_pack(12582912.0f, 12582912.0f)), r0, r1);
+                        } else {
+                            const float u0 = __saturatef(fmaf(p.x, f0, p.y));
+                            const float u1 = __saturatef(fmaf(p.z, f1, p.w));
+                            f2_unpack(f2_fma(f2_pack(u0, u1), f2_pack(255.0f, 255.0f),
+                                             f2_pack(8388608.0f, 8388608.0f)), r0, r1);
+                        }
+                        b[2 * e] = __float_as_uint(r0);
+                        b[2 * e + 1] = __float_as_uint(r1);
+                    }
+                    wd[j] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+                }
+                if (m < rows) {
+                    if (TRANS) {
+                        // next block input, group-major [c_out / 32][N * HW / 4][32]
+                        int8_t* o = static_cast<int8_t*>(a.out) + (static_cast<size_t>(c0 >> 5) * rows + m) * 32;
+                        *reinterpret_cast<uint4*>(o) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                        *reinterpret_cast<uint4*>(o + 16) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
+                    } else {
+                        uint8_t* o = static_cast<uint8_t*>(a.out);
+                        const int plane = c0 >> 4;
+                        *reinterpret_cast<uint4*>(o + (static_cast<size_t>(plane) * rows + m) * 16) =
+                            make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                        *reinterpret_cast<uint4*>(o + (static_cast<size_t>(plane + 1) * rows + m) * 16) =
+                            make_uint4(wd[4], wd[5], wd[6], wd[7]);
+                    }
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_free(tmem, tcols);
+    }
+}
+
+template <bool F16, bool TRANS>
+static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st) {
+    const size_t smem = gemm_layout(TRANS, g.G, g.nc, g.nchunks, g.raw_bytes, &g.sb, &g.b_resident) + 1024;
+    if (smem > 227 * 1024 || g.sb < 2) return cudaErrorInvalidConfiguration;
+    const int ntiles = ((g.rows + 127) / 128) * g.nchunks;
+    const int grid = ntiles < sms ? ntiles : sms;
+    if (grid <= 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, TRANS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    gemm_kernel<F16, TRANS><<<grid, GM_THREADS, smem, st>>>(g);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st) {
+    GemmArgs g{};
+    g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
+    g.out = a.out; g.err = a.err;
+    g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.HW; g.W = 0;
+    g.rows = a.N * a.HW; g.cout = 128; g.nc = 128; g.nchunks = 1;
+    g.raw_bytes = 4 * 4096;
+    return a.prologue_f16 ? launch_gemm<true, false>(g, sms, st) : launch_gemm<false, false>(g, sms, st);
+}
+
+// output channels per CTA tile: 256 when it divides c_out (TMEM: 2 x 256 columns), else 128
+int trans_chunk(int cout) { return cout % 256 == 0 ? 256 : 128; }
+
+// Largest raw span of a transition tile: its 128 consecutive pooled pixels cover at most
+// 128 / W2 pooled rows when W2 divides 128 (tiles start on a row), else ceil(128 / W2) + 1;
+// each pooled row needs two whole input rows.
+static int trans_raw_bytes(int W) {
+    const int W2 = W / 2;
+    const int prow = (128 % W2 == 0) ? 128 / W2 : (128 + W2 - 1) / W2 + 1;
+    return ((2 * prow * W * 32 + 1023) / 1024) * 1024;
+}
+
+cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st) {
+    GemmArgs g{};
+    const int cout = a.G * 16;
+    g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
+    g.out = a.out; g.err = a.err;
+    g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.H * a.W; g.W = a.W;
+    g.rows = a.N * (a.H / 2) * (a.W / 2); g.cout = cout; g.nc = trans_chunk(cout); g.nchunks = cout / g.nc;
+    g.raw_bytes = trans_raw_bytes(a.W);
+    return a.prologue_f16 ? launch_gemm<true, true>(g, sms, st) : launch_gemm<false, true>(g, sms, st);
+}
+
+}  // namespace dn8

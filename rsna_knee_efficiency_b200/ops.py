@@ -6,6 +6,7 @@ C ABI of include/dn8.h). Layouts:
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import _native as nat
@@ -32,3 +33,39 @@ def conv2(x: torch.Tensor, w2k: torch.Tensor, sc: torch.Tensor, out: torch.Tenso
           W: int, err: torch.Tensor | None = None, stream=None) -> None:
     a = nat.Conv2Args(_ptr(x), _ptr(w2k), _ptr(sc), _ptr(out), _ptr(err), N, H, W)
     nat.check(nat.lib().dn8_conv2(a, _stream(stream)), "dn8_conv2")
+
+
+def trans(in0: torch.Tensor, seg: torch.Tensor, tw: torch.Tensor, ab: torch.Tensor, gd: torch.Tensor,
+          out: torch.Tensor, G0: int, G: int, N: int, H: int, W: int, prologue_f16: bool,
+          err: torch.Tensor | None = None, stream=None) -> None:
+    a = nat.TransArgs(_ptr(in0), _ptr(seg), _ptr(tw), _ptr(ab), _ptr(gd), _ptr(out), _ptr(err),
+                      G0, G, N, H, W, int(bool(prologue_f16)))
+    nat.check(nat.lib().dn8_trans(a, _stream(stream)), "dn8_trans")
+
+
+# --- weight preparation (numpy in, numpy out) ----------------------------------------------
+def prepare_conv1_weights(w1: np.ndarray) -> np.ndarray:
+    """`L*_w1` [G, 128, 32] int8 -> the UMMA-ready table (G * 4096 bytes)."""
+    w1 = np.ascontiguousarray(w1, dtype=np.int8)
+    out = np.empty(w1.shape[0] * 4096, np.uint8)
+    nat.check(nat.lib().dn8_prepare_conv1_weights(w1.ctypes.data, w1.shape[0], out.ctypes.data),
+              "dn8_prepare_conv1_weights")
+    return out
+
+
+def prepare_trans_weights(tw: np.ndarray) -> np.ndarray:
+    """`T*_w` [G, c_out, 32] int8 -> the UMMA-ready table (G * c_out * 32 bytes)."""
+    tw = np.ascontiguousarray(tw, dtype=np.int8)
+    out = np.empty(tw.size, np.uint8)
+    nat.check(nat.lib().dn8_prepare_trans_weights(tw.ctypes.data, tw.shape[0], tw.shape[1],
+                                                  out.ctypes.data), "dn8_prepare_trans_weights")
+    return out
+
+
+def prepare_conv2_weights(w2k: np.ndarray) -> np.ndarray:
+    """`L*_w2k` [4, 9, 32, 32] int8 -> the conv2 operand table (36864 bytes)."""
+    w2k = np.ascontiguousarray(w2k, dtype=np.int8)
+    out = np.empty(36864, np.uint8)
+    nat.check(nat.lib().dn8_prepare_conv2_weights(w2k.ctypes.data, out.ctypes.data),
+              "dn8_prepare_conv2_weights")
+    return out

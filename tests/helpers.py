@@ -32,9 +32,9 @@ def rand_store(rng: np.random.Generator, shape, kind: str = "uniform") -> np.nda
 
 
 def split_store(X: np.ndarray, c0: int):
-    """Channel-last store X [N, HW, c] -> (in0 [N, G0, HW, 32], seg [L, N, HW, 32])."""
+    """Channel-last store X [N, HW, c] -> (in0 [G0, N, HW, 32] group-major, seg [L, N, HW, 32])."""
     N, HW, c = X.shape
-    in0 = X[..., :c0].reshape(N, HW, c0 // 32, 32).transpose(0, 2, 1, 3)
+    in0 = X[..., :c0].reshape(N, HW, c0 // 32, 32).transpose(2, 0, 1, 3)
     L = (c - c0) // 32
     seg = X[..., c0:].reshape(N, HW, L, 32).transpose(2, 0, 1, 3)
     return np.ascontiguousarray(in0), np.ascontiguousarray(seg)

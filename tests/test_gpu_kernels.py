@@ -28,7 +28,8 @@ def _conv1_case(par, bi, li, c0, N, HW, f16, kind, seed):
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     segd = dev(seg) if li > 0 else torch.zeros(16, dtype=torch.int8, device="cuda")
     tab = par[f"L{bi}_{li}_abh"] if f16 else par[f"L{bi}_{li}_ab"]
-    ops.conv1(dev(in0), segd, dev(par[f"L{bi}_{li}_w1"]), dev(tab), dev(par[f"L{bi}_{li}_gdu"]),
+    ops.conv1(dev(in0), segd, dev(ops.prepare_conv1_weights(par[f"L{bi}_{li}_w1"])), dev(tab),
+              dev(par[f"L{bi}_{li}_gdu"]),
               out, c0 // 32, cin // 32, N, HW, f16, err=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -63,7 +64,8 @@ def _conv2_case(par, bi, li, N, H, W, seed):
     rows = N * H * W
     out = torch.full((rows * 32,), 0x5A, dtype=torch.int8, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    ops.conv2(dev(pixels_to_planes(V.reshape(rows, 128))), dev(par[f"L{bi}_{li}_w2k"]),
+    ops.conv2(dev(pixels_to_planes(V.reshape(rows, 128))),
+              dev(ops.prepare_conv2_weights(par[f"L{bi}_{li}_w2k"])),
               dev(par[f"L{bi}_{li}_c2u"]), out, N, H, W, err=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -84,4 +86,43 @@ def test_conv2_ref_layers_512(bi, li):
 def test_conv2_small_and_ragged(N, H, W):
     _, _, par = plan_tables(512)
     got, want = _conv2_case(par, 1, 2, N, H, W, N * 1000 + H * 10 + W)
+    np.testing.assert_array_equal(got, want)
+
+
+def _trans_case(par, plan, bi, N, H, W, f16, kind, seed):
+    rng = np.random.default_rng(seed)
+    b = plan.blocks[bi]
+    c0, ctot = b.c0, b.c_tot
+    X = rand_store(rng, (N, H * W, ctot), kind)
+    in0, seg = split_store(X, c0)
+    cout = ctot // 2
+    out = torch.full((N * cout * (H // 2) * (W // 2),), 0x33, dtype=torch.int8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    tab = par[f"T{bi}_abh"] if f16 else par[f"T{bi}_ab"]
+    ops.trans(dev(in0), dev(seg), dev(ops.prepare_trans_weights(par[f"T{bi}_w"])), dev(tab),
+              dev(par[f"T{bi}_gd"]), out, c0 // 32, ctot // 32, N, H, W, f16, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    # next block's group-major in0 [G0n][N][HW/4][32] -> channel-last [N, H/2, W/2, cout]
+    got = out.view(cout // 32, N, (H // 2) * (W // 2), 32).permute(1, 2, 0, 3).reshape(
+        N, H // 2, W // 2, cout).cpu().numpy()
+    want = orc.trans(X.reshape(N, H, W, ctot), par[f"T{bi}_w"],
+                     ab=None if f16 else par[f"T{bi}_ab"], abh=par[f"T{bi}_abh"] if f16 else None,
+                     gd=par[f"T{bi}_gd"], mode=orc.KERNEL)
+    return got, want
+
+
+@pytest.mark.parametrize("bi", [0, 1, 2])
+@pytest.mark.parametrize("f16", [True, False])
+def test_trans_512(bi, f16):
+    _, plan, par = plan_tables(512)
+    b = plan.blocks[bi]
+    got, want = _trans_case(par, plan, bi, 2, b.h, b.w, f16, "uniform", 900 + bi)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("bi,N,H,W", [(0, 3, 6, 10), (2, 2, 4, 4), (1, 1, 2, 2), (2, 5, 8, 6)])
+def test_trans_small_and_ragged(bi, N, H, W):
+    _, plan, par = plan_tables(512)
+    got, want = _trans_case(par, plan, bi, N, H, W, True, "relu", 31 * bi + N + H + W)
     np.testing.assert_array_equal(got, want)
