@@ -93,12 +93,53 @@ typedef struct dn8_trans_args {
 } dn8_trans_args;
 int dn8_trans(const dn8_trans_args* a, dn8_stream stream);
 
+/* stem: replaces the reference's TensorRT fp16 stem + `quant_seg` and its exact INT8 form
+ * `stem_i8` (src/knee/dense8s_kernels.cu:3641-3771, formula `stem_q_i8` src/knee/dense8s.py:625-643),
+ * fused with the input producer `gather_u8_to_f16` (src/knee/data/fused_uint8.py:480-505).
+ * Pixels: x_u8 = 0: fp16 windows [N][3][H][W], u = rint(255 sat(x)); x_u8 = 1: uint8 planes
+ * [P][H][W] gathered through src[N][4] = {plane of channel 0, 1, 2, unused}, u = the byte.
+ * flags[n] bit 0 (optional array): horizontal flip of image n. 7x7/2 pad-3 conv with the int8
+ * weights, q = rint(clamp(fmaf(acc, k_o, c_o), 0, 127)) (S_kc = [k(64), c(64)]), 3x3/2 pad-1
+ * max-pool, into block 1's group-major input [2][N][H/4 * W/4][32]. H, W multiples of 4, W <= 512. */
+typedef struct dn8_stem_args {
+    const void* x;
+    const int32_t* src;    /* x_u8 = 1: [N][4] plane indices */
+    const int32_t* flags;  /* [N] or NULL */
+    const int8_t* w;       /* S_w8 [64][176] after dn8_prepare_stem_weights (12288 bytes) */
+    const float* kc;       /* S_kc [128] */
+    int8_t* out;
+    int32_t* err;
+    int32_t N, H, W;
+    int32_t x_u8;
+} dn8_stem_args;
+int dn8_stem(const dn8_stem_args* a, dn8_stream stream);
+
+/* global pooling + linear head: replaces `final_q` (reference :2304-2323, launched at
+ * src/knee/dense8s.py:1379-1385) and adds the benchmark head (linear C -> n_out, mean over the
+ * slices of a view). features = mean over pixels of relu(a_c q + b_c) (F_ab, the reference's
+ * summation order); logits = features . Hw^T + Hb (fp32); view_logits[v] = mean of the logits of
+ * images v*per_view .. v*per_view + per_view - 1. One CTA per image. */
+typedef struct dn8_head_args {
+    const int8_t* in0;      /* last block's input groups, group-major [G0][N][HW][32] */
+    const int8_t* seg;      /* its layer segments [L][N][HW][32] */
+    const float* fab;       /* F_ab [C][2] */
+    float* feat;            /* [N][C] float, or NULL */
+    const float* hw;        /* [n_out][C] float, or NULL (no head) */
+    const float* hb;        /* [n_out] */
+    float* logits;          /* [N][n_out] */
+    float* view_logits;     /* [N / per_view][n_out], or NULL */
+    int32_t* tickets;       /* [N / per_view] zero-initialised device counters (left zeroed) */
+    int32_t G0, G, N, HW, n_out, per_view;
+} dn8_head_args;
+int dn8_head(const dn8_head_args* a, dn8_stream stream);
+
 /* ---- weight preparation (host memory to host memory, once per pack) ------------------------
  * The kernels read their weights with bulk copies straight into the tensor cores' shared-memory
  * operand layout; these functions permute the reference pack tables into that layout. */
 int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out);               /* G*4096 B */
 int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out); /* G*cout*32 B */
 int dn8_prepare_conv2_weights(const int8_t* w2k, uint8_t* out);                         /* 36864 B */
+int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out);                           /* 12288 B */
 
 const char* dn8_last_error(void);   /* message of the calling thread's last failed call */
 int dn8_device_sms(int device);     /* SM count used to size persistent grids (0 on error) */

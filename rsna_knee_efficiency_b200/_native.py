@@ -26,10 +26,24 @@ class TransArgs(ctypes.Structure):
                 ("G0", I32), ("G", I32), ("N", I32), ("H", I32), ("W", I32), ("prologue_f16", I32)]
 
 
+class StemArgs(ctypes.Structure):
+    _fields_ = [("x", P), ("src", P), ("flags", P), ("w", P), ("kc", P), ("out", P), ("err", P),
+                ("N", I32), ("H", I32), ("W", I32), ("x_u8", I32)]
+
+
+class HeadArgs(ctypes.Structure):
+    _fields_ = [("in0", P), ("seg", P), ("fab", P), ("feat", P), ("hw", P), ("hb", P),
+                ("logits", P), ("view_logits", P), ("tickets", P),
+                ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("n_out", I32), ("per_view", I32)]
+
+
 EXPORTS = {
     "dn8_conv1": ([ctypes.POINTER(Conv1Args), P], ctypes.c_int),
     "dn8_conv2": ([ctypes.POINTER(Conv2Args), P], ctypes.c_int),
     "dn8_trans": ([ctypes.POINTER(TransArgs), P], ctypes.c_int),
+    "dn8_stem": ([ctypes.POINTER(StemArgs), P], ctypes.c_int),
+    "dn8_head": ([ctypes.POINTER(HeadArgs), P], ctypes.c_int),
+    "dn8_prepare_stem_weights": ([P, P], ctypes.c_int),
     "dn8_prepare_conv1_weights": ([P, I32, P], ctypes.c_int),
     "dn8_prepare_trans_weights": ([P, I32, I32, P], ctypes.c_int),
     "dn8_prepare_conv2_weights": ([P, P], ctypes.c_int),

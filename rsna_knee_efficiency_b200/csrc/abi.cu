@@ -130,6 +130,48 @@ int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t
     return DN8_OK;
 }
 
+int dn8_stem(const dn8_stem_args* a, dn8_stream stream) {
+    if (a == nullptr) return fail(DN8_EINVAL, "dn8_stem: null arguments");
+    if (a->N < 1 || a->H < 4 || a->W < 4 || a->H % 4 || a->W % 4 || a->W > 512)
+        return fail(DN8_EINVAL, "dn8_stem: unsupported geometry N=%d H=%d W=%d (multiples of 4, W <= 512)", a->N,
+                    a->H, a->W);
+    if (a->x == nullptr || !aligned16(a->w) || a->kc == nullptr || !aligned16(a->out) || (a->x_u8 && a->src == nullptr))
+        return fail(DN8_EINVAL, "dn8_stem: bad pointers");
+    int sms = 0;
+    if (int s = current_sms(&sms)) return s;
+    cudaError_t e = dn8::launch_stem(*a, sms, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_stem launch");
+}
+
+int dn8_head(const dn8_head_args* a, dn8_stream stream) {
+    if (a == nullptr) return fail(DN8_EINVAL, "dn8_head: null arguments");
+    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64)
+        return fail(DN8_EINVAL, "dn8_head: bad geometry");
+    if (!aligned16(a->in0) || !aligned16(a->seg) || a->fab == nullptr)
+        return fail(DN8_EINVAL, "dn8_head: bad pointers");
+    if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
+        return fail(DN8_EINVAL, "dn8_head: head without bias or logits buffer");
+    if (a->view_logits != nullptr && (a->per_view < 1 || a->N % a->per_view || a->tickets == nullptr))
+        return fail(DN8_EINVAL, "dn8_head: views need per_view dividing N and a ticket array");
+    cudaError_t e = dn8::launch_head(*a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_head launch");
+}
+
+int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out) {
+    if (w8 == nullptr || out == nullptr) return fail(DN8_EINVAL, "dn8_prepare_stem_weights: bad arguments");
+    // S_w8 [64][176] -> 6 K steps of [64 rows][32 B], K bytes 176 .. 191 zero, 32B-swizzled
+    int8_t tile[64 * 32];
+    for (int kk = 0; kk < 6; ++kk) {
+        for (int o = 0; o < 64; ++o)
+            for (int c = 0; c < 32; ++c) {
+                const int k = kk * 32 + c;
+                tile[o * 32 + c] = k < 176 ? w8[o * 176 + k] : 0;
+            }
+        swizzle32_tile(tile, 64, out + kk * 2048);
+    }
+    return DN8_OK;
+}
+
 int dn8_prepare_conv2_weights(const int8_t* w2k, uint8_t* out) {
     if (w2k == nullptr || out == nullptr) return fail(DN8_EINVAL, "dn8_prepare_conv2_weights: bad arguments");
     // w2k [cblk][tap][o][32] -> [dy][cblk][half][dx * 32 + o][16] (tap = 3 dy + dx)

@@ -4,6 +4,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #define DN8_DEV __device__ __forceinline__
@@ -227,6 +228,16 @@ DN8_DEV uint32_t prologue_f32x4(uint32_t q4, const float2* ab) {
         r |= prologue_f32(q, ab[k].x, ab[k].y) << (8 * k);
     }
     return r;
+}
+
+// Two fp16 pixels (one half2 word) -> two u8 in the low 16 bits: rint(255 sat(x)) computed in fp32
+// (the reference's `u8pair`, dense8s_kernels.cu:3631-3639).
+DN8_DEV uint32_t u8_of_f16x2(uint32_t h2) {
+    const float a = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+    const float b = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16)));
+    const uint32_t qa = __float_as_uint(fmaf(__saturatef(a), 255.0f, 12582912.0f));
+    const uint32_t qb = __float_as_uint(fmaf(__saturatef(b), 255.0f, 12582912.0f));
+    return __byte_perm(qa, qb, 0x0040) & 0xFFFFu;
 }
 
 // conv1 epilogue (u8 bottleneck): rint(255 sat(fmaf(g, acc, d))) (reference :598-611).

@@ -10,6 +10,8 @@ namespace dn8 {
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st);
 cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st);
 int trans_chunk(int cout);
+cudaError_t launch_stem(const dn8_stem_args& a, int sms, cudaStream_t st);
+cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st);
 
 struct Conv2Plan {
     CUtensorMap map;      // bottleneck planes, built once per geometry and buffer

@@ -1,0 +1,107 @@
+// head.cu -- global pooling of the last block (norm5 with sigma folded, ReLU, spatial mean) and the
+// linear head in one reduction kernel: one CTA per image.
+//   features f[n][c] = (p0 + p1 + p2 + p3) / HW with p_q the fp32 sum, in ascending pixel order, of
+//     relu(fmaf(a_c, q, b_c)) over pixels s = q, q + 4, ...: the reference's `final_q`
+//     (src/knee/dense8s_kernels.cu:2306-2323), bit for bit;
+//   logits l[n][j] = sum_c f[n][c] * Hw[j][c] + Hb[j] (fp32, fixed reduction order);
+//   per view of V consecutive images the mean of the logits over the view (the slice mean), written
+//   by the last CTA of the view to finish (an atomic ticket per view, reset for the next call).
+#include "dn8_common.cuh"
+#include "dn8_kernels.h"
+
+namespace dn8 {
+
+constexpr int HD_THREADS = 512;
+
+__global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args a) {
+    extern __shared__ float hs[];
+    const int C = a.G * 32, HW = a.HW, n = blockIdx.x;
+    float* part = hs;                          // [4][C]
+    float* feat = hs + 4 * C;                  // [C]
+    float* red = feat + C;                     // [HD_THREADS / 32][NOUT]
+    const int tid = threadIdx.x;
+    // task = (group g, half h, partial q): 16 channels, pixels q, q + 4, ...
+    for (int task = tid; task < a.G * 8; task += HD_THREADS) {
+        const int g = task >> 3, h = (task >> 2) & 1, q = task & 3;
+        const int8_t* base = g < a.G0 ? a.in0 + ((static_cast<size_t>(g) * a.N + n) * HW) * 32
+                                      : a.seg + ((static_cast<size_t>(g - a.G0) * a.N + n) * HW) * 32;
+        base += h * 16;
+        const float2* ab = reinterpret_cast<const float2*>(a.fab) + g * 32 + h * 16;
+        float av[16], bv[16], acc[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const float2 p = ab[k];
+            av[k] = p.x;
+            bv[k] = p.y;
+            acc[k] = 0.0f;
+        }
+        for (int s = q; s < HW; s += 4) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + static_cast<size_t>(s) * 32));
+            const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                // the byte q + 128 in the mantissa of 2^23: exact float q
+                const float f = __int_as_float(__byte_perm(w[k >> 2], 0x4B000000u, 0x7540 | (k & 3))) - 8388736.0f;
+                acc[k] += fmaxf(fmaf(av[k], f, bv[k]), 0.0f);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) part[q * C + g * 32 + h * 16 + k] = acc[k];
+    }
+    __syncthreads();
+    for (int c = tid; c < C; c += HD_THREADS) {
+        const float f = (part[c] + part[C + c] + part[2 * C + c] + part[3 * C + c]) / static_cast<float>(HW);
+        feat[c] = f;
+        if (a.feat != nullptr) a.feat[static_cast<size_t>(n) * C + c] = f;
+    }
+    __syncthreads();
+    if (a.hw == nullptr) return;
+    // logits: each warp reduces a strided share of the channels for every output, then a fixed tree
+    const int warp = tid >> 5, lane = tid & 31, nw = HD_THREADS / 32;
+    for (int j = 0; j < a.n_out; ++j) {
+        float s = 0.0f;
+        for (int c = tid; c < C; c += HD_THREADS) s = fmaf(feat[c], a.hw[static_cast<size_t>(j) * C + c], s);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) red[warp * a.n_out + j] = s;
+    }
+    __syncthreads();
+    if (tid < a.n_out) {
+        float s = 0.0f;
+        for (int w = 0; w < nw; ++w) s += red[w * a.n_out + tid];
+        a.logits[static_cast<size_t>(n) * a.n_out + tid] = s + a.hb[tid];
+    }
+    if (a.view_logits == nullptr || a.per_view < 1) return;
+    // the last image of a view to finish averages the view's logits in image order
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    const int v = n / a.per_view;
+    if (tid == 0) {
+        const int ticket = atomicAdd(a.tickets + v, 1);
+        s_last = ticket == a.per_view - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        if (tid < a.n_out) {
+            float s = 0.0f;
+            for (int k = 0; k < a.per_view; ++k)
+                s += __ldcg(a.logits + static_cast<size_t>(v * a.per_view + k) * a.n_out + tid);
+            a.view_logits[static_cast<size_t>(v) * a.n_out + tid] = s / static_cast<float>(a.per_view);
+        }
+        if (tid == 0) a.tickets[v] = 0;
+    }
+}
+
+cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st) {
+    const int C = a.G * 32;
+    const size_t smem = (static_cast<size_t>(5) * C + (HD_THREADS / 32) * (a.n_out > 0 ? a.n_out : 1)) * sizeof(float);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    head_kernel<<<a.N, HD_THREADS, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace dn8

@@ -43,7 +43,36 @@ def trans(in0: torch.Tensor, seg: torch.Tensor, tw: torch.Tensor, ab: torch.Tens
     nat.check(nat.lib().dn8_trans(a, _stream(stream)), "dn8_trans")
 
 
+def stem(x: torch.Tensor, w8u: torch.Tensor, kc: torch.Tensor, out: torch.Tensor, N: int, H: int,
+         W: int, src: torch.Tensor | None = None, flags: torch.Tensor | None = None,
+         err: torch.Tensor | None = None, stream=None) -> None:
+    """x: fp16 [N, 3, H, W] windows, or uint8 planes [P, H, W] with `src` int32 [N, 4]."""
+    x_u8 = x.dtype == torch.uint8
+    a = nat.StemArgs(_ptr(x), _ptr(src), _ptr(flags), _ptr(w8u), _ptr(kc), _ptr(out), _ptr(err),
+                     N, H, W, int(x_u8))
+    nat.check(nat.lib().dn8_stem(a, _stream(stream)), "dn8_stem")
+
+
+def head(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: int, N: int, HW: int,
+         feat: torch.Tensor | None = None, hw: torch.Tensor | None = None, hb: torch.Tensor | None = None,
+         logits: torch.Tensor | None = None, view_logits: torch.Tensor | None = None,
+         tickets: torch.Tensor | None = None, per_view: int = 0, stream=None) -> None:
+    n_out = 0 if hw is None else hw.shape[0]
+    a = nat.HeadArgs(_ptr(in0), _ptr(seg), _ptr(fab), _ptr(feat), _ptr(hw), _ptr(hb), _ptr(logits),
+                     _ptr(view_logits), _ptr(tickets), G0, G, N, HW, n_out, per_view)
+    nat.check(nat.lib().dn8_head(a, _stream(stream)), "dn8_head")
+
+
 # --- weight preparation (numpy in, numpy out) ----------------------------------------------
+def prepare_stem_weights(w8: np.ndarray) -> np.ndarray:
+    """`S_w8` [64, 176] int8 -> the stem operand table (12288 bytes)."""
+    w8 = np.ascontiguousarray(w8, dtype=np.int8)
+    out = np.empty(12288, np.uint8)
+    nat.check(nat.lib().dn8_prepare_stem_weights(w8.ctypes.data, out.ctypes.data),
+              "dn8_prepare_stem_weights")
+    return out
+
+
 def prepare_conv1_weights(w1: np.ndarray) -> np.ndarray:
     """`L*_w1` [G, 128, 32] int8 -> the UMMA-ready table (G * 4096 bytes)."""
     w1 = np.ascontiguousarray(w1, dtype=np.int8)

@@ -126,3 +126,74 @@ def test_trans_small_and_ragged(bi, N, H, W):
     _, plan, par = plan_tables(512)
     got, want = _trans_case(par, plan, bi, N, H, W, True, "relu", 31 * bi + N + H + W)
     np.testing.assert_array_equal(got, want)
+
+
+def _stem_case(par, x, flip, u8_planes):
+    N, _, H, W = x.shape
+    PH, PW = H // 4, W // 4
+    out = torch.full((2 * N * PH * PW * 32,), 0x11, dtype=torch.int8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    flags = None if flip is None else dev(np.asarray(flip, np.int32))
+    w8u, kc = dev(ops.prepare_stem_weights(par["S_w8"])), dev(par["S_kc"])
+    if u8_planes:
+        src = np.zeros((N, 4), np.int32)
+        src[:, :3] = np.arange(3 * N).reshape(N, 3)
+        ops.stem(dev(x.reshape(3 * N, H, W)), w8u, kc, out, N, H, W, src=dev(src), flags=flags, err=err)
+    else:
+        ops.stem(dev(x), w8u, kc, out, N, H, W, flags=flags, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    # group-major [2][N][PH*PW][32] -> channel-last [N, PH, PW, 64]
+    got = out.view(2, N, PH * PW, 32).permute(1, 2, 0, 3).reshape(N, PH, PW, 64).cpu().numpy()
+    want = orc.stem(x, par["S_w8f"], par["S_kc"], flip=flip, mode=orc.KERNEL)
+    return got, want
+
+
+@pytest.mark.parametrize("u8_planes", [True, False])
+@pytest.mark.parametrize("flip", [None, [1, 0, 1]])
+def test_stem_512(u8_planes, flip):
+    from rsna_knee_efficiency_b200 import synth
+    _, _, par = plan_tables(512)
+    t = synth.triplets(synth.volume(5))[[0, 11, 23]]
+    x = t if u8_planes else (t.astype(np.float32) / 255.0).astype(np.float16)
+    got, want = _stem_case(par, x, flip, u8_planes)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("H,W", [(64, 64), (32, 96), (128, 128), (16, 24)])
+def test_stem_small_and_fp16_off_grid(H, W):
+    """Small images, and fp16 pixels that are not k/255 (zoomed / interpolated windows)."""
+    _, _, par = plan_tables(512)
+    rng = np.random.default_rng(H * W)
+    x = rng.uniform(-0.05, 1.05, size=(2, 3, H, W)).astype(np.float16)
+    got, want = _stem_case(par, x, [0, 1], False)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("N,HW", [(3, 256), (2, 4), (5, 16)])
+def test_head(N, HW):
+    _, plan, par = plan_tables(512)
+    from rsna_knee_efficiency_b200 import densenet
+    b = plan.blocks[3]
+    rng = np.random.default_rng(N + HW)
+    X = rand_store(rng, (N, HW, b.c_tot), "uniform")
+    in0, seg = split_store(X, b.c0)
+    head = densenet.random_head(3)
+    hw = head.fc.weight.detach().numpy().astype(np.float32)
+    hb = head.fc.bias.detach().numpy().astype(np.float32)
+    feat = torch.zeros((N, b.c_tot), dtype=torch.float32, device="cuda")
+    logits = torch.zeros((N, 4), dtype=torch.float32, device="cuda")
+    per_view = 1 if N % 2 else 2
+    views = torch.zeros((N // per_view, 4), dtype=torch.float32, device="cuda")
+    tickets = torch.zeros(N // per_view, dtype=torch.int32, device="cuda")
+    for _ in range(2):                                   # tickets must come back zeroed
+        ops.head(dev(in0), dev(seg), dev(par["F_ab"]), b.c0 // 32, b.c_tot // 32, N, HW, feat=feat,
+                 hw=dev(hw), hb=dev(hb), logits=logits, view_logits=views, tickets=tickets,
+                 per_view=per_view)
+    torch.cuda.synchronize()
+    want_f = orc.final(X, par["F_ab"], orc.KERNEL)
+    np.testing.assert_array_equal(feat.cpu().numpy(), want_f)        # bit-exact features
+    want_l = orc.head(want_f, hw, hb)
+    np.testing.assert_allclose(logits.cpu().numpy(), want_l, rtol=0, atol=1e-5)
+    np.testing.assert_allclose(views.cpu().numpy(), want_l.reshape(-1, per_view, 4).mean(1), rtol=0, atol=1e-5)
+    assert int(tickets.abs().sum().item()) == 0
