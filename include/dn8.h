@@ -111,6 +111,7 @@ typedef struct dn8_stem_args {
     int32_t* err;
     int32_t N, H, W;
     int32_t x_u8;
+    int32_t n_alloc;       /* images the output groups are laid out for (>= N; 0 = N) */
 } dn8_stem_args;
 int dn8_stem(const dn8_stem_args* a, dn8_stream stream);
 
@@ -130,6 +131,7 @@ typedef struct dn8_head_args {
     float* view_logits;     /* [N / per_view][n_out], or NULL */
     int32_t* tickets;       /* [N / per_view] zero-initialised device counters (left zeroed) */
     int32_t G0, G, N, HW, n_out, per_view;
+    int32_t n_alloc;        /* images the store groups are laid out for (>= N; 0 = N) */
 } dn8_head_args;
 int dn8_head(const dn8_head_args* a, dn8_stream stream);
 
@@ -140,6 +142,52 @@ int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out);       
 int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out); /* G*cout*32 B */
 int dn8_prepare_conv2_weights(const int8_t* w2k, uint8_t* out);                         /* 36864 B */
 int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out);                           /* 12288 B */
+
+/* ---- engine level ------------------------------------------------------------------------- */
+
+typedef struct dn8_table {  /* one pack table, by the reference's name (`kernel_params`) */
+    const char* name;       /* e.g. "L0_3_w1", "T1_abh", "F_ab", "S_w8", "S_kc", "H_w" */
+    const void* data;       /* host memory, the reference's layout and dtype */
+    int64_t nbytes;
+} dn8_table;
+
+typedef struct dn8_pack_desc {  /* the pack `meta` (src/knee/dense8s.py:810-831) as plain fields */
+    int32_t n;              /* images per pass (meta "n") */
+    int32_t img, in_ch, n_blocks;
+    int32_t c0[4], h[4], w[4], L[4], trans[4];
+    int32_t trans_f16[4];   /* transition prologue: 1 = T*_abh (fp16), 0 = T*_ab (fp32) */
+    const int8_t* c1_f16[4];/* per dense layer: 1 = L*_abh (fp16 prologue), 0 = L*_ab */
+    int32_t n_out;          /* head outputs (tables H_w, H_b); 0 = features only */
+    const dn8_table* tables;
+    int32_t n_tables;
+} dn8_pack_desc;
+
+typedef struct dn8_engine dn8_engine;
+
+typedef struct dn8_input {  /* the pixels of one forward call */
+    const void* x;          /* x_u8 = 0: fp16 [n][3][img][img]; x_u8 = 1: uint8 planes [P][img][img] */
+    const int32_t* src;     /* x_u8 = 1: device [n][4] plane indices of the 3 channels (+ unused) */
+    const int32_t* flags;   /* device [n] (bit 0: horizontal flip) or NULL */
+    int32_t x_u8;
+} dn8_input;
+
+/* Validates and uploads the pack; allocates arenas for `n` images per pass on `device`. */
+int dn8_engine_create(const dn8_pack_desc* pack, int device, dn8_engine** out);
+void dn8_engine_destroy(dn8_engine* e);
+/* Enqueues ceil(n / pass) passes on `stream`: features [n][C] (float, NULL to skip), logits
+ * [n][n_out] and view_logits [n / per_view][n_out] (NULL to skip). All pointers are device
+ * pointers. No allocation and no host synchronisation: capturable in a CUDA graph. */
+int dn8_engine_forward(dn8_engine* e, const dn8_input* in, int32_t n, float* feat, float* logits,
+                       float* view_logits, int32_t per_view, dn8_stream stream);
+/* Synchronises `stream`, then reads (and clears) the device error word: DN8_EDEVICE if a kernel gave
+ * up a bounded wait since the last check. */
+int dn8_engine_check(dn8_engine* e, dn8_stream stream);
+/* Copies store segment j of block b (j = 0: the block input groups [G0][n][HW][32]; j >= 1: the
+ * output of dense layer j-1, [n][HW][32]) to dst (device or host memory). Valid for the last two
+ * blocks of the last pass (blocks alternate between two arenas). */
+int dn8_engine_store(const dn8_engine* e, int32_t block, int32_t j, int8_t* dst, dn8_stream stream);
+const char* dn8_engine_error(const dn8_engine* e);
+int64_t dn8_engine_device_bytes(const dn8_engine* e);
 
 const char* dn8_last_error(void);   /* message of the calling thread's last failed call */
 int dn8_device_sms(int device);     /* SM count used to size persistent grids (0 on error) */

@@ -28,13 +28,29 @@ class TransArgs(ctypes.Structure):
 
 class StemArgs(ctypes.Structure):
     _fields_ = [("x", P), ("src", P), ("flags", P), ("w", P), ("kc", P), ("out", P), ("err", P),
-                ("N", I32), ("H", I32), ("W", I32), ("x_u8", I32)]
+                ("N", I32), ("H", I32), ("W", I32), ("x_u8", I32), ("n_alloc", I32)]
 
 
 class HeadArgs(ctypes.Structure):
     _fields_ = [("in0", P), ("seg", P), ("fab", P), ("feat", P), ("hw", P), ("hb", P),
                 ("logits", P), ("view_logits", P), ("tickets", P),
-                ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("n_out", I32), ("per_view", I32)]
+                ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("n_out", I32), ("per_view", I32),
+                ("n_alloc", I32)]
+
+
+class Table(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("data", P), ("nbytes", ctypes.c_int64)]
+
+
+class PackDesc(ctypes.Structure):
+    _fields_ = [("n", I32), ("img", I32), ("in_ch", I32), ("n_blocks", I32),
+                ("c0", I32 * 4), ("h", I32 * 4), ("w", I32 * 4), ("L", I32 * 4), ("trans", I32 * 4),
+                ("trans_f16", I32 * 4), ("c1_f16", P * 4), ("n_out", I32),
+                ("tables", ctypes.POINTER(Table)), ("n_tables", I32)]
+
+
+class Input(ctypes.Structure):
+    _fields_ = [("x", P), ("src", P), ("flags", P), ("x_u8", I32)]
 
 
 EXPORTS = {
@@ -47,6 +63,13 @@ EXPORTS = {
     "dn8_prepare_conv1_weights": ([P, I32, P], ctypes.c_int),
     "dn8_prepare_trans_weights": ([P, I32, I32, P], ctypes.c_int),
     "dn8_prepare_conv2_weights": ([P, P], ctypes.c_int),
+    "dn8_engine_create": ([ctypes.POINTER(PackDesc), ctypes.c_int, ctypes.POINTER(P)], ctypes.c_int),
+    "dn8_engine_destroy": ([P], None),
+    "dn8_engine_forward": ([P, ctypes.POINTER(Input), I32, P, P, P, I32, P], ctypes.c_int),
+    "dn8_engine_check": ([P, P], ctypes.c_int),
+    "dn8_engine_store": ([P, I32, I32, P, P], ctypes.c_int),
+    "dn8_engine_error": ([P], ctypes.c_char_p),
+    "dn8_engine_device_bytes": ([P], ctypes.c_int64),
     "dn8_last_error": ([], ctypes.c_char_p),
     "dn8_device_sms": ([ctypes.c_int], ctypes.c_int),
 }
@@ -73,10 +96,11 @@ class Dn8Error(RuntimeError):
     pass
 
 
-def check(status: int, what: str) -> None:
+def check(status: int, what: str, engine=None) -> None:
     if status == DN8_OK:
         return
-    msg = lib().dn8_last_error().decode(errors="replace")
+    src = lib().dn8_engine_error(engine) if engine else lib().dn8_last_error()
+    msg = src.decode(errors="replace")
     if status == DN8_EINVAL:
         raise ValueError(f"{what}: {msg}")
     raise Dn8Error(f"{what} (status {status}): {msg}")

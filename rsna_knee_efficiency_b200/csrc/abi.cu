@@ -52,6 +52,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 extern "C" {
 
 const char* dn8_last_error(void) { return g_last_error.c_str(); }
+void dn8_set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
 int dn8_device_sms(int device) {
     int sms = 0;

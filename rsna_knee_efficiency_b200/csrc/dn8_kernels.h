@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include "../../include/dn8.h"
 
+extern "C" void dn8_set_last_error(const char* msg);   // thread-local message channel (abi.cu)
+
 namespace dn8 {
 
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st);

@@ -16,6 +16,7 @@ constexpr int HD_THREADS = 512;
 __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args a) {
     extern __shared__ float hs[];
     const int C = a.G * 32, HW = a.HW, n = blockIdx.x;
+    const size_t nal = static_cast<size_t>(a.n_alloc > a.N ? a.n_alloc : a.N);
     float* part = hs;                          // [4][C]
     float* feat = hs + 4 * C;                  // [C]
     float* red = feat + C;                     // [HD_THREADS / 32][NOUT]
@@ -23,8 +24,8 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
     // task = (group g, half h, partial q): 16 channels, pixels q, q + 4, ...
     for (int task = tid; task < a.G * 8; task += HD_THREADS) {
         const int g = task >> 3, h = (task >> 2) & 1, q = task & 3;
-        const int8_t* base = g < a.G0 ? a.in0 + ((static_cast<size_t>(g) * a.N + n) * HW) * 32
-                                      : a.seg + ((static_cast<size_t>(g - a.G0) * a.N + n) * HW) * 32;
+        const int8_t* base = g < a.G0 ? a.in0 + ((static_cast<size_t>(g) * nal + n) * HW) * 32
+                                      : a.seg + ((static_cast<size_t>(g - a.G0) * nal + n) * HW) * 32;
         base += h * 16;
         const float2* ab = reinterpret_cast<const float2*>(a.fab) + g * 32 + h * 16;
         float av[16], bv[16], acc[16];

@@ -361,7 +361,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         }
                         // block 1 input, group-major [2][N][PH * PW][32]
                         const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
-                        const size_t gstride = static_cast<size_t>(geo.N) * PH * PW * 32;
+                        const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
                         int8_t* o = a.out + pix * 32;
                         *reinterpret_cast<uint4*>(o) = make_uint4(mx[0], mx[1], mx[2], mx[3]);
                         *reinterpret_cast<uint4*>(o + 16) = make_uint4(mx[4], mx[5], mx[6], mx[7]);

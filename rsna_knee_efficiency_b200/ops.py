@@ -49,7 +49,7 @@ def stem(x: torch.Tensor, w8u: torch.Tensor, kc: torch.Tensor, out: torch.Tensor
     """x: fp16 [N, 3, H, W] windows, or uint8 planes [P, H, W] with `src` int32 [N, 4]."""
     x_u8 = x.dtype == torch.uint8
     a = nat.StemArgs(_ptr(x), _ptr(src), _ptr(flags), _ptr(w8u), _ptr(kc), _ptr(out), _ptr(err),
-                     N, H, W, int(x_u8))
+                     N, H, W, int(x_u8), 0)
     nat.check(nat.lib().dn8_stem(a, _stream(stream)), "dn8_stem")
 
 
@@ -59,7 +59,7 @@ def head(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: in
          tickets: torch.Tensor | None = None, per_view: int = 0, stream=None) -> None:
     n_out = 0 if hw is None else hw.shape[0]
     a = nat.HeadArgs(_ptr(in0), _ptr(seg), _ptr(fab), _ptr(feat), _ptr(hw), _ptr(hb), _ptr(logits),
-                     _ptr(view_logits), _ptr(tickets), G0, G, N, HW, n_out, per_view)
+                     _ptr(view_logits), _ptr(tickets), G0, G, N, HW, n_out, per_view, 0)
     nat.check(nat.lib().dn8_head(a, _stream(stream)), "dn8_head")
 
 
