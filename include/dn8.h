@@ -186,6 +186,20 @@ int dn8_engine_check(dn8_engine* e, dn8_stream stream);
  * output of dense layer j-1, [n][HW][32]) to dst (device or host memory). Valid for the last two
  * blocks of the last pass (blocks alternate between two arenas). */
 int dn8_engine_store(const dn8_engine* e, int32_t block, int32_t j, int8_t* dst, dn8_stream stream);
+/* One pass of n (<= pass size) images with a CUDA event after every launch (the reference's
+ * `Dense8SEncoder.profile`, src/knee/dense8s.py:1548-1563): out[k] = kind, block, layer and device
+ * milliseconds of launch k, *n_launches = launches of the pass. Synchronises `stream`. */
+#define DN8_K_STEM 0
+#define DN8_K_CONV1 1
+#define DN8_K_CONV2 2
+#define DN8_K_TRANS 3
+#define DN8_K_HEAD 4
+typedef struct dn8_launch_info {
+    int32_t kind, block, layer;
+    float ms;
+} dn8_launch_info;
+int dn8_engine_profile(dn8_engine* e, const dn8_input* in, int32_t n, float* feat, dn8_launch_info* out,
+                       int32_t max_out, int32_t* n_launches, dn8_stream stream);
 const char* dn8_engine_error(const dn8_engine* e);
 int64_t dn8_engine_device_bytes(const dn8_engine* e);
 

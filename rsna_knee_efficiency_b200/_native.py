@@ -53,6 +53,12 @@ class Input(ctypes.Structure):
     _fields_ = [("x", P), ("src", P), ("flags", P), ("x_u8", I32)]
 
 
+class LaunchInfo(ctypes.Structure):
+    _fields_ = [("kind", I32), ("block", I32), ("layer", I32), ("ms", ctypes.c_float)]
+
+
+KIND_NAMES = {0: "stem", 1: "conv1", 2: "conv2", 3: "trans", 4: "head"}
+
 EXPORTS = {
     "dn8_conv1": ([ctypes.POINTER(Conv1Args), P], ctypes.c_int),
     "dn8_conv2": ([ctypes.POINTER(Conv2Args), P], ctypes.c_int),
@@ -67,6 +73,8 @@ EXPORTS = {
     "dn8_engine_destroy": ([P], None),
     "dn8_engine_forward": ([P, ctypes.POINTER(Input), I32, P, P, P, I32, P], ctypes.c_int),
     "dn8_engine_check": ([P, P], ctypes.c_int),
+    "dn8_engine_profile": ([P, ctypes.POINTER(Input), I32, P, ctypes.POINTER(LaunchInfo), I32,
+                            ctypes.POINTER(I32), P], ctypes.c_int),
     "dn8_engine_store": ([P, I32, I32, P, P], ctypes.c_int),
     "dn8_engine_error": ([P], ctypes.c_char_p),
     "dn8_engine_device_bytes": ([P], ctypes.c_int64),

@@ -36,6 +36,10 @@ struct dn8_engine {
     const float* hw = nullptr; const float* hb = nullptr;
     dn8::Conv2Plan c2plan[4];
     std::string error;
+    // profiling: an event after every launch of one pass, with (kind, block, layer) of the launch
+    std::vector<cudaEvent_t> events;
+    std::vector<dn8_launch_info> rec;
+    bool profiling = false;
 };
 
 namespace {
@@ -72,6 +76,7 @@ void dn8_engine_destroy(dn8_engine* e) {
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(e->device);
+    for (cudaEvent_t ev : e->events) cudaEventDestroy(ev);
     cudaFree(e->tables);
     cudaFree(e->arena[0]);
     cudaFree(e->arena[1]);
@@ -116,7 +121,6 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
 
     // ---- host staging of every prepared table, then one device copy ----
     std::vector<uint8_t> stage;
-    std::vector<std::pair<size_t*, size_t>> fix;          // (pointer slot offset, offset) fixed up after upload
     auto reserve = [&](size_t bytes) {
         const size_t off = align256(stage.size());
         stage.resize(off + bytes);
@@ -259,6 +263,15 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
     return DN8_OK;
 }
 
+// In profiling mode, records an event after a launch of (kind, block, layer).
+static void mark(dn8_engine* e, int kind, int block, int layer, cudaStream_t st) {
+    if (!e->profiling) return;
+    const size_t i = e->rec.size();
+    if (i + 1 >= e->events.size()) return;
+    cudaEventRecord(e->events[i + 1], st);
+    e->rec.push_back({kind, block, layer, 0.0f});
+}
+
 // One pass of up to n_cap images (images [0, n) of the pass are real).
 static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, float* feat, float* logits,
                        float* view_logits, int per_view, cudaStream_t st) {
@@ -274,6 +287,7 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
         s.w = reinterpret_cast<const int8_t*>(e->sw); s.kc = e->kc; s.out = e->arena[0]; s.err = e->err;
         s.N = n; s.H = e->img; s.W = e->img; s.x_u8 = in->x_u8; s.n_alloc = cap;
         if ((ce = dn8::launch_stem(s, e->sms, st)) != cudaSuccess) return efail(e, DN8_ECUDA, "stem: %s", cudaGetErrorString(ce));
+        mark(e, DN8_K_STEM, 0, 0, st);
     }
     for (int b = 0; b < e->n_blocks; ++b) {
         const int HW = e->h[b] * e->w[b], G0 = e->c0[b] / 32;
@@ -287,12 +301,14 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
             c1.prologue_f16 = e->c1_f16[b][l];
             if ((ce = dn8::launch_conv1(c1, e->sms, st)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv1 b%d l%d: %s", b, l, cudaGetErrorString(ce));
+            mark(e, DN8_K_CONV1, b, l, st);
             dn8_conv2_args c2{};
             c2.x = e->bott; c2.w = reinterpret_cast<const int8_t*>(ly.w2); c2.sc = ly.c2;
             c2.out = seg + static_cast<size_t>(l) * cap * HW * 32; c2.err = e->err;
             c2.N = cap; c2.H = e->h[b]; c2.W = e->w[b];
             if ((ce = dn8::launch_conv2(e->c2plan[b], c2, e->sms, st)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv2 b%d l%d: %s", b, l, cudaGetErrorString(ce));
+            mark(e, DN8_K_CONV2, b, l, st);
         }
         if (e->trans[b]) {
             dn8_trans_args t{};
@@ -301,6 +317,7 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
             t.G0 = G0; t.G = G0 + e->L[b]; t.N = cap; t.H = e->h[b]; t.W = e->w[b]; t.prologue_f16 = e->trans_f16[b];
             if ((ce = dn8::launch_trans(t, e->sms, st)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "transition %d: %s", b, cudaGetErrorString(ce));
+            mark(e, DN8_K_TRANS, b, 0, st);
         } else {
             dn8_head_args hd{};
             hd.in0 = in0; hd.seg = seg; hd.fab = e->fab;
@@ -314,6 +331,7 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
             hd.G0 = G0; hd.G = G0 + e->L[b]; hd.N = n; hd.HW = HW; hd.n_out = e->n_out; hd.per_view = per_view;
             hd.n_alloc = cap;
             if ((ce = dn8::launch_head(hd, st)) != cudaSuccess) return efail(e, DN8_ECUDA, "head: %s", cudaGetErrorString(ce));
+            mark(e, DN8_K_HEAD, b, 0, st);
         }
     }
     return DN8_OK;
@@ -332,6 +350,37 @@ int dn8_engine_forward(dn8_engine* e, const dn8_input* in, int32_t n, float* fea
     for (int img0 = 0; img0 < n && rc == DN8_OK; img0 += e->n)
         rc = engine_pass(e, in, img0, std::min(e->n, n - img0), feat, logits, view_logits, per_view,
                          static_cast<cudaStream_t>(stream));
+    if (prev != e->device) cudaSetDevice(prev);
+    return rc;
+}
+
+int dn8_engine_profile(dn8_engine* e, const dn8_input* in, int32_t n, float* feat, dn8_launch_info* out,
+                       int32_t max_out, int32_t* n_launches, dn8_stream stream) {
+    if (e == nullptr || in == nullptr || out == nullptr || n_launches == nullptr || n < 1 || n > e->n)
+        return efail(e, DN8_EINVAL, "profile: bad arguments (n must fit one pass)");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != e->device) cudaSetDevice(e->device);
+    if (e->events.empty()) {
+        e->events.resize(512);
+        for (cudaEvent_t& ev : e->events) cudaEventCreate(&ev);
+    }
+    e->rec.clear();
+    e->profiling = true;
+    cudaEventRecord(e->events[0], st);
+    int rc = engine_pass(e, in, 0, n, feat, nullptr, nullptr, 0, st);
+    e->profiling = false;
+    cudaError_t ce = cudaStreamSynchronize(st);
+    if (rc == DN8_OK && ce != cudaSuccess) rc = efail(e, DN8_ECUDA, "profile: %s", cudaGetErrorString(ce));
+    int k = 0;
+    for (; rc == DN8_OK && k < static_cast<int>(e->rec.size()) && k < max_out; ++k) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, e->events[k], e->events[k + 1]);
+        out[k] = e->rec[k];
+        out[k].ms = ms;
+    }
+    *n_launches = k;
     if (prev != e->device) cudaSetDevice(prev);
     return rc;
 }

@@ -213,3 +213,27 @@ class Dense8SEncoder:
         self.stream.synchronize()
         t = buf.view(groups, self.nb, hw, 32).permute(1, 0, 3, 2).reshape(self.nb, groups * 32, b["h"], b["w"])
         return t.float()
+
+    def profile(self, x: torch.Tensor | None = None, planes=None, src=None, flags=None,
+                reps: int = 3) -> list:
+        """Device milliseconds of every launch of one pass (averaged over `reps` passes after a
+        warm-up), from CUDA events between launches: [(kind, block, layer, ms)] (the reference's
+        `profile`, dense8s.py:1548-1563)."""
+        if x is not None:
+            xh = x[:self.nb].to(self.in_dtype).contiguous()
+            inp, n = nat.Input(xh.data_ptr(), None, None, 0), xh.shape[0]
+        else:
+            inp = nat.Input(planes.data_ptr(), src.data_ptr(), None if flags is None else flags.data_ptr(), 1)
+            n = min(self.nb, src.shape[0])
+        buf = (nat.LaunchInfo * 512)()
+        cnt = nat.I32()
+        acc = None
+        for r in range(reps + 1):
+            nat.check(nat.lib().dn8_engine_profile(self._h, ctypes.byref(inp), n, self.out.data_ptr(), buf,
+                                                   512, ctypes.byref(cnt), self.stream.cuda_stream),
+                      "dn8_engine_profile", self._h)
+            if r == 0:
+                continue
+            row = [(nat.KIND_NAMES[buf[k].kind], buf[k].block, buf[k].layer, buf[k].ms) for k in range(cnt.value)]
+            acc = row if acc is None else [(a[0], a[1], a[2], a[3] + b[3]) for a, b in zip(acc, row)]
+        return [(k, b, l, ms / reps) for k, b, l, ms in acc]

@@ -1,0 +1,90 @@
+"""Study-level inference over the INT8 encoders: the part of the reference's inference loop
+(src/knee/infer.py:974-1110, `_model_logits_budget_u8`, `_seed_logits_views_u8`, `_forward_split`)
+that drives the encoder, restated for the benchmark's study workload.
+
+A study has two crop windows (two uint8 volumes of S slices); every seed reads ONE of them (the
+reference's complementary half-window budget, src/knee/window_budget.py:57-123: seed k reads
+window k % 2). Each window gives S - 2 slice triplets (stride 1, depth 3); the stem gathers them
+straight from the uint8 planes (the reference's `gather_u8_f16` fused into the stem), optionally
+adding the horizontally flipped copy of every triplet (flip TTA). Per seed the head's logits are
+averaged over the view's images; the study logits are the mean over seeds. Studies are independent:
+ranks take contiguous shards with no collective on the data path, and the host gathers the logits.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .encoder import Dense8SEncoder
+
+DEPTH = 3
+
+
+def shard(n_items: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, end) share of rank `rank` (the reference splits studies per GPU the same
+    way, infer.py:1065-1110)."""
+    per = -(-n_items // world)
+    start = min(n_items, rank * per)
+    return start, min(n_items, start + per)
+
+
+class StudyRunner:
+    """Two (or more) seeds' encoders on one GPU, fed `studies` studies per call.
+
+    `volumes` given to `run` is uint8 [n_windows, studies, S, H, W] on the device (window-major, so
+    the planes of one window of all the call's studies are contiguous)."""
+
+    def __init__(self, packs: list[dict], dev: int, studies: int, slices: int = 26,
+                 flip_tta: bool = False) -> None:
+        self.dev, self.studies, self.slices, self.flip_tta = dev, studies, slices, flip_tta
+        self.n_win = slices - DEPTH + 1
+        self.per_view = self.n_win * (2 if flip_tta else 1)
+        self.n_img = studies * self.per_view
+        self.encoders = [Dense8SEncoder(p, dev, self.n_img) for p in packs]
+        for e in self.encoders:
+            if e.n_head < 1:
+                raise ValueError("StudyRunner needs packs with a head (H_w, H_b)")
+        self.n_out = self.encoders[0].n_head
+        d = f"cuda:{dev}"
+        # plane table: image (study s, triplet i[, flipped]) reads planes s*S + i, +1, +2
+        src, flags = [], []
+        for s in range(studies):
+            for f in ((0, 1) if flip_tta else (0,)):
+                for i in range(self.n_win):
+                    src.append([s * slices + i, s * slices + i + 1, s * slices + i + 2, 0])
+                    flags.append(f)
+        self.src = torch.tensor(src, dtype=torch.int32, device=d)
+        self.flags = torch.tensor(flags, dtype=torch.int32, device=d) if flip_tta else None
+        self.logits = [torch.zeros((self.n_img, self.n_out), dtype=torch.float32, device=d) for _ in packs]
+        self.views = [torch.zeros((studies, self.n_out), dtype=torch.float32, device=d) for _ in packs]
+        self.out = torch.zeros((studies, self.n_out), dtype=torch.float32, device=d)
+
+    @property
+    def launches_per_call(self) -> int:
+        per_pass = 2 + 2 * sum(b["L"] for b in self.encoders[0].meta["blocks"]) + \
+            sum(1 for b in self.encoders[0].meta["blocks"] if b["trans"])
+        passes = -(-self.n_img // self.encoders[0].nb)
+        return per_pass * passes * len(self.encoders)
+
+    def run(self, volumes: torch.Tensor) -> torch.Tensor:
+        """Study logits [studies, n_out] (the mean over seeds of each seed's view mean)."""
+        nwin, S = volumes.shape[0], volumes.shape[1]
+        if S != self.studies or volumes.dtype != torch.uint8:
+            raise ValueError(f"volumes {tuple(volumes.shape)} {volumes.dtype}: expected uint8 "
+                             f"[windows, {self.studies}, slices, H, W]")
+        for k, enc in enumerate(self.encoders):
+            planes = volumes[k % nwin].reshape(-1, volumes.shape[-2], volumes.shape[-1])
+            enc.encode_u8(planes, self.src, self.flags, self.logits[k], self.views[k], self.per_view)
+        torch.stack(self.views).mean(0, out=self.out)
+        return self.out
+
+
+def make_volumes(n_studies: int, windows: int = 2, img: int = 512, slices: int = 26, seed: int = 0):
+    """uint8 [windows, n_studies, slices, img, img]: study s window w from synthetic volume seed
+    seed + 2 s + w."""
+    from .synth import volume
+    out = np.empty((windows, n_studies, slices, img, img), np.uint8)
+    for s in range(n_studies):
+        for w in range(windows):
+            out[w, s] = volume(seed + 2 * s + w, S=slices, H=img, W=img)
+    return out
