@@ -245,7 +245,7 @@ def main():
         return
     import torch
     import torch.distributed as dist
-    from rsna_knee_efficiency_b200.infer import StudyRunner, make_volumes
+    from rsna_knee_efficiency_b200.infer import StudyRunner, make_volumes, run_shard
     torch.cuda.set_device(local)
     dev = f"cuda:{local}"
     if world > 1:
@@ -286,18 +286,18 @@ def main():
         ev1.record()
         barrier()
     ms = ev0.elapsed_time(ev1)
-    # ---- e2e: public API with host buffers (H2D of the step's volumes, D2H of the logits) ----
-    stage = torch.empty((2, S) + tuple(vol_host.shape[2:]), dtype=torch.uint8, device=dev)
-    host_out = torch.empty((args.steps, S, runner.n_out), dtype=torch.float32).pin_memory()
+    # ---- e2e: the public study loop (`run_shard`) from pinned host volumes: every step copies its
+    # studies' volumes host -> device (overlapped with the previous step's encoders) and reads the
+    # study logits back into pinned host memory ----
+    order = torch.arange(args.steps * S) % pool
+    host_all = vol_host[:, order].pin_memory()                  # [2, steps*S, slices, H, W]
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.steps):
-        b = i % blocks_per_pool
-        stage.copy_(vol_host[:, b * S:(b + 1) * S], non_blocking=True)
-        host_out[i].copy_(runner.run(stage), non_blocking=True)
+    logits_e2e = run_shard(runner, host_all)
     e1.record()
     barrier()
+    assert logits_e2e.shape == (args.steps * S, runner.n_out) and bool(torch.isfinite(logits_e2e).all())
     ms_e2e = e0.elapsed_time(e1)
     for e in runner.encoders:
         e.check()

@@ -79,7 +79,7 @@ int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream);
  * (src/knee/dense8s.py:1242-1272). Prologue as conv1 on all G = c_tot / 32 groups, 1x1 conv
  * c_tot -> c_tot / 2, the four accumulators of every 2x2 square summed exactly (int32), then
  * q = rint(clamp(k_o * s, +-127)), k = T*_gd[o][0], into the next block's group-major in0
- * [c_tot/64][N][H*W/4][32]. H and W even. */
+ * [c_tot/64][N][H*W/4][32]. c_tot a multiple of 256 (G % 8 == 0), H and W even. */
 typedef struct dn8_trans_args {
     const int8_t* in0;
     const int8_t* seg;

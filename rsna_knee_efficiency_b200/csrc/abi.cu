@@ -49,10 +49,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace dn8 {
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace dn8
+
 extern "C" {
 
 const char* dn8_last_error(void) { return g_last_error.c_str(); }
-void dn8_set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
 int dn8_device_sms(int device) {
     int sms = 0;
@@ -92,7 +95,7 @@ int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream) {
 
 int dn8_trans(const dn8_trans_args* a, dn8_stream stream) {
     if (a == nullptr) return fail(DN8_EINVAL, "dn8_trans: null arguments");
-    if (a->G < 2 || a->G % 2 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->H < 2 || a->W < 2 || a->H % 2 ||
+    if (a->G < 8 || a->G % 8 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->H < 2 || a->W < 2 || a->H % 2 ||
         a->W % 2)
         return fail(DN8_EINVAL, "dn8_trans: bad geometry G0=%d G=%d N=%d H=%d W=%d", a->G0, a->G, a->N, a->H, a->W);
     if (a->G * 16 > 640) return fail(DN8_EINVAL, "dn8_trans: c_out %d > 640", a->G * 16);
@@ -120,7 +123,7 @@ int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out) {
 }
 
 int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out) {
-    if (tw == nullptr || out == nullptr || G < 1 || cout < 32 || cout % 32)
+    if (tw == nullptr || out == nullptr || G < 1 || cout < 128 || cout % 128)
         return fail(DN8_EINVAL, "dn8_prepare_trans_weights: bad arguments");
     const int nc = dn8::trans_chunk(cout), nchunks = cout / nc;
     // [nchunks][G][nc rows][32]: chunk c holds output channels c * nc .. c * nc + nc - 1

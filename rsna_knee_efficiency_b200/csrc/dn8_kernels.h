@@ -5,9 +5,9 @@
 #include <cuda_runtime.h>
 #include "../../include/dn8.h"
 
-extern "C" void dn8_set_last_error(const char* msg);   // thread-local message channel (abi.cu)
-
 namespace dn8 {
+
+__attribute__((visibility("hidden"))) void set_last_error(const char* msg);  // thread-local message (abi.cu)
 
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st);
 cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st);

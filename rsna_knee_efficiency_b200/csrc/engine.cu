@@ -97,7 +97,7 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
             std::string msg = e->error;
             dn8_engine_destroy(e);
             // keep the message reachable through the thread-local channel of the kernel level
-            dn8_set_last_error(msg.c_str());
+            dn8::set_last_error(msg.c_str());
         }
         return code;
     };
@@ -109,7 +109,7 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
         e->c0[b] = p->c0[b]; e->h[b] = p->h[b]; e->w[b] = p->w[b]; e->L[b] = p->L[b];
         e->trans[b] = p->trans[b]; e->trans_f16[b] = p->trans_f16[b];
         if (p->c0[b] % 32 || p->L[b] < 1 || p->h[b] < 1 || p->w[b] < 1 || p->w[b] > 128 ||
-            (p->trans[b] && ((p->c0[b] + 32 * p->L[b]) % 64 || p->h[b] % 2 || p->w[b] % 2)))
+            (p->trans[b] && ((p->c0[b] + 32 * p->L[b]) % 256 || p->h[b] % 2 || p->w[b] % 2)))
             return bail(efail(e, DN8_EINVAL, "block %d geometry c0=%d L=%d h=%d w=%d not supported", b, p->c0[b],
                               p->L[b], p->h[b], p->w[b]));
         e->c1_f16[b].assign(p->c1_f16[b], p->c1_f16[b] + p->L[b]);

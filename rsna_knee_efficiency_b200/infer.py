@@ -45,7 +45,7 @@ class StudyRunner:
             if e.n_head < 1:
                 raise ValueError("StudyRunner needs packs with a head (H_w, H_b)")
         self.n_out = self.encoders[0].n_head
-        d = f"cuda:{dev}"
+        d = self.device = f"cuda:{dev}"
         # plane table: image (study s, triplet i[, flipped]) reads planes s*S + i, +1, +2
         src, flags = [], []
         for s in range(studies):
@@ -75,8 +75,82 @@ class StudyRunner:
         for k, enc in enumerate(self.encoders):
             planes = volumes[k % nwin].reshape(-1, volumes.shape[-2], volumes.shape[-1])
             enc.encode_u8(planes, self.src, self.flags, self.logits[k], self.views[k], self.per_view)
-        torch.stack(self.views).mean(0, out=self.out)
+        torch.mean(torch.stack(self.views), 0, out=self.out)
         return self.out
+
+
+def run_shard(runner, volumes, rank: int = 0, world: int = 1) -> torch.Tensor:
+    """Study logits [n_local, n_out] (float32, host) of this rank's contiguous shard of `volumes`
+    (uint8 [windows, n_studies, S, H, W] in host memory, pinned for overlap): batches of
+    `runner.studies` studies are copied to the device on a copy stream (two staging buffers, the
+    next batch's copy overlapping this batch's encoders), run, and their logits read back into
+    pinned host memory; the last batch is padded by repeating its last study. `runner` needs
+    `studies`, `device`, `n_out` and `run(volumes_on_device)` (on the current stream)."""
+    n = volumes.shape[1]
+    start, end = shard(n, world, rank)
+    vols = torch.as_tensor(volumes)
+    B, dev = runner.studies, runner.device
+    starts = list(range(start, end, B))
+    on_gpu = str(dev).startswith("cuda")
+    out = torch.empty((end - start, runner.n_out), dtype=torch.float32, pin_memory=on_gpu)
+    shape = (vols.shape[0], B) + tuple(vols.shape[2:])
+    stages = [torch.empty(shape, dtype=torch.uint8, device=dev) for _ in range(2 if on_gpu else 1)]
+
+    def fill(st, s0):
+        k = min(B, end - s0)
+        for w in range(st.shape[0]):                 # one contiguous copy per window
+            st[w, :k].copy_(vols[w, s0:s0 + k], non_blocking=True)
+        if k < B:
+            st[:, k:].copy_(st[:, k - 1:k].expand(-1, B - k, *st.shape[2:]))
+        return k
+
+    if not on_gpu:
+        for s0 in starts:
+            k = fill(stages[0], s0)
+            out[s0 - start:s0 - start + k].copy_(runner.run(stages[0])[:k])
+        return out
+    cur = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    loaded = [torch.cuda.Event() for _ in stages]
+    freed: list = [None, None]
+    copy.wait_stream(cur)
+
+    def load(j):
+        with torch.cuda.stream(copy):
+            if freed[j & 1] is not None:
+                copy.wait_event(freed[j & 1])
+            fill(stages[j & 1], starts[j])
+            loaded[j & 1].record(copy)
+
+    if starts:
+        load(0)
+    for j, s0 in enumerate(starts):
+        if j + 1 < len(starts):
+            load(j + 1)
+        cur.wait_event(loaded[j & 1])
+        logits = runner.run(stages[j & 1])
+        freed[j & 1] = torch.cuda.Event()
+        freed[j & 1].record(cur)
+        k = min(B, end - s0)
+        out[s0 - start:s0 - start + k].copy_(logits[:k], non_blocking=True)
+    cur.synchronize()
+    return out
+
+
+def gather_logits(local: torch.Tensor, n_studies: int, device=None) -> torch.Tensor:
+    """All ranks' shard logits, in study order [n_studies, n_out], on every rank (one all_gather of
+    the padded shards; the only collective of the study path, outside the timed data path)."""
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return local
+    world = dist.get_world_size()
+    per = -(-n_studies // world)
+    pad = torch.zeros((per, local.shape[1]), dtype=local.dtype, device=device or local.device)
+    pad[:local.shape[0]].copy_(local)
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad)
+    rows = [p[:shard(n_studies, world, r)[1] - shard(n_studies, world, r)[0]] for r, p in enumerate(parts)]
+    return torch.cat(rows).to(local.device)
 
 
 def make_volumes(n_studies: int, windows: int = 2, img: int = 512, slices: int = 26, seed: int = 0):
