@@ -35,6 +35,7 @@ os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))   # oracle th
 
 METRIC = "INT8 DenseNet169 512px images/s & studies/s at 1/2/4/8 B200; % per-layer roofline"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def parse():
@@ -53,11 +54,13 @@ def parse():
 
 
 def peaks():
+    """(HBM GB/s, dense INT8 TOP/s, source). The INT8 peak is taken as twice the measured dense bf16
+    GEMM throughput (the tensor core's INT8 rate is twice its bf16 rate)."""
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return FALLBACK_HBM_GBS, "fallback"
+        return float(d["hbm_gbs"]), 2 * float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, 2 * FALLBACK_BF16_TFLOPS, "fallback"
 
 
 # ---- clocks during the timed region ------------------------------------------------------------
@@ -175,7 +178,7 @@ def run_reference(args, rank: int):
 
 
 # ---- the GPU arm ------------------------------------------------------------------------------
-def build_packs(img: int, dev: str):
+def build_packs(img: int, dev: str, n: int):
     import torch
     from rsna_knee_efficiency_b200 import densenet, pack as packmod, quant, synth
     packs = []
@@ -184,55 +187,66 @@ def build_packs(img: int, dev: str):
         batches = [torch.from_numpy(b).to(dev) for b in synth.calibration_batches(8, 4, img, seed=1000 + seed)]
         cal = quant.calibrate(m, batches, method="pct", pct=99.99)
         plan = quant.make_plan(m.cpu(), cal, img)
-        packs.append(packmod.make_pack(plan, 192, densenet.random_head(seed)))
+        packs.append(packmod.make_pack(plan, n, densenet.random_head(seed)))
     return packs
 
 
-def conv1_roofline(enc, runner, hbm_gbs: float, peak_kind: str, vol_dev):
-    """conv1 (all 82 layers of one pass) from the engine's per-launch CUDA events: algorithmic bytes
-    = rows * (c_in + 128) per layer (store read once, bottleneck written once) + the weights."""
+def launch_work(kind: str, blk: dict, l: int, n: int, img: int) -> tuple[float, float]:
+    """(algorithmic HBM bytes, MACs) of one launch over n images: every tensor read or written once.
+    conv1: store c_in + bottleneck 128 per pixel (+ weights); conv2: bottleneck 128 + slot 32 per
+    pixel (+ weights); transition: c_tot per input pixel read, c_tot / 2 per pooled pixel written,
+    MACs of the exact integer form (four 1x1 outputs per pooled pixel); stem: the three uint8 planes
+    read and block 1's 64-channel input written, 7x7x3 MACs per conv output; head: last store read."""
+    hw = blk["h"] * blk["w"]
+    if kind == "conv1":
+        cin = blk["c0"] + 32 * l
+        return n * hw * (cin + 128) + cin * 128, n * hw * 128 * cin
+    if kind == "conv2":
+        return n * hw * 160 + 36864, n * hw * 32 * 1152
+    ctot = blk["c0"] + 32 * blk["L"]
+    if kind == "trans":
+        return n * hw * ctot + n * hw // 4 * ctot // 2, n * hw * ctot * ctot // 2
+    if kind == "stem":
+        return n * (3 * img * img + 64 * hw), n * (img // 2) ** 2 * 64 * 147
+    return n * hw * ctot, 0
+
+
+def roofline(enc, runner, hbm_gbs: float, i8_tops: float, peak_kind: str, vol_dev):
+    """From the engine's per-launch CUDA events (one pass, averaged over 3): the dominant kernel
+    (conv1, all 82 layers: achieved = its algorithmic bytes / its time, against the measured HBM
+    copy bandwidth) and, per kernel family / block and for the whole pass, the fraction
+    t_roof / t_measured with t_roof = max(bytes / HBM, 2 MACs / INT8 peak) per launch."""
     prof = enc.profile(planes=vol_dev[0].reshape(-1, vol_dev.shape[-2], vol_dev.shape[-1]), src=runner.src,
                        flags=runner.flags, reps=3)
     blocks = enc.meta["blocks"]
-    n = enc.nb
-    tot_b = tot_ms = 0.0
-    per_kind = {}
+    n, img = enc.nb, enc.in_shape[2]
+    per = {}
     for kind, b, l, ms in prof:
-        blk = blocks[b]
-        hw = blk["h"] * blk["w"]
-        if kind == "conv1":
-            cin = blk["c0"] + 32 * l
-            by = n * hw * (cin + 128) + cin * 128
-            tot_b += by
-            tot_ms += ms
-        elif kind == "conv2":
-            by = n * hw * (128 + 32) + 36864
-        elif kind == "trans":
-            ctot = blk["c0"] + 32 * blk["L"]
-            by = n * hw * ctot + n * hw // 4 * ctot // 2
-        elif kind == "stem":
-            by = n * (3 * enc.in_shape[2] ** 2 + 64 * hw)       # uint8 pixels read, block-1 input written
-        else:
-            by = n * hw * (blk["c0"] + 32 * blk["L"])
-        k = per_kind.setdefault(kind, [0.0, 0.0, 0])
-        k[0] += by
-        k[1] += ms
-        k[2] += 1
-    achieved = tot_b / (tot_ms * 1e-3) / 1e9
+        by, macs = launch_work(kind, blocks[b], l, n, img)
+        t_roof = max(by / (hbm_gbs * 1e9), 2 * macs / (i8_tops * 1e12)) * 1e3
+        for key in (kind, f"{kind}.b{b}"):
+            k = per.setdefault(key, [0.0, 0.0, 0.0, 0])
+            k[0] += by
+            k[1] += ms
+            k[2] += t_roof
+            k[3] += 1
+    c1 = per["conv1"]
+    achieved = c1[0] / (c1[1] * 1e-3) / 1e9
     traffic = None
-    tf = ROOT / "profiles" / "conv1_traffic.json"
+    tf = ROOT / "profiles" / "dram_traffic_encoder_512_b192.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
-    summary = {k: {"launches": v[2], "ms": round(v[1], 3), "GBps": round(v[0] / (v[1] * 1e-3) / 1e9, 1),
-                   "frac": round(v[0] / (v[1] * 1e-3) / 1e9 / hbm_gbs, 3)} for k, v in per_kind.items()}
-    roof_ms = sum(v[0] for v in per_kind.values()) / (hbm_gbs * 1e9) * 1e3
-    pass_ms = sum(v[1] for v in per_kind.values())
+        traffic = json.loads(tf.read_text()).get("conv1_dram_bytes_per_pass")
+    summary = {k: {"launches": v[3], "ms": round(v[1], 3), "GBps": round(v[0] / (v[1] * 1e-3) / 1e9, 1),
+                   "roof_ms": round(v[2], 4), "frac": round(v[2] / v[1], 3)} for k, v in per.items()}
+    kinds = [v for k, v in per.items() if "." not in k]
+    roof_ms = sum(v[2] for v in kinds)
+    pass_ms = sum(v[1] for v in kinds)
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
             "frac": round(achieved / hbm_gbs, 4), "traffic": traffic, "peak_source": peak_kind,
-            "kernel": "conv1 (gemm_kernel, 82 launches of one pass)",
-            "algorithmic_bytes_per_pass": int(tot_b),
+            "kernel": "conv1 (gemm_kernel, all 82 launches of one pass; traffic per pass)",
+            "algorithmic_bytes_per_pass": int(c1[0]),
             "network": {"frac": round(roof_ms / pass_ms, 4), "pass_ms": round(pass_ms, 3),
-                        "roof_ms": round(roof_ms, 3), "per_kind": summary}}
+                        "roof_ms": round(roof_ms, 3), "int8_tops": i8_tops, "per_kind": summary}}
 
 
 def main():
@@ -253,8 +267,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device(dev))
     # setup (untimed): packs, engines, the resident pool of synthetic studies
-    packs = build_packs(args.img, dev)
     S = args.studies
+    per_view = 24 * (2 if args.flip_tta else 1)
+    packs = build_packs(args.img, dev, S * per_view)        # one pass per seed per step
     pool = max(S, (args.pool or S) // S * S)
     vol_host = torch.from_numpy(make_volumes(pool, img=args.img, seed=10_000 * (rank + 1))).pin_memory()
     vol_dev = vol_host.to(dev)
@@ -315,8 +330,8 @@ def main():
     e2e = imgs_per_step * steps_e2e * world / (ms_e2e * 1e-3)
     clocks = clk.summary()
     if rank == 0:
-        hbm, kind = peaks()
-        roof = conv1_roofline(runner.encoders[0], runner, hbm, kind, vol_dev)
+        hbm, i8, kind = peaks()
+        roof = roofline(runner.encoders[0], runner, hbm, i8, kind, vol_dev)
         cpu = None
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(args.cpu_seconds, args.img)

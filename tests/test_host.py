@@ -62,21 +62,31 @@ def test_synthetic_volume_is_seeded():
 
 
 def test_calibrate_percentile_is_exact_order_statistic():
-    """pct calibration = the ceil((1 - q) n)-th largest |x| over all batches (per channel for the
-    stored segments), checked against a direct sort on a tiny network input."""
+    """pct calibration = the ceil((1 - q) n)-th largest |x| over the union of all batches: per
+    tensor for the conv inputs, per channel for the stored segments; checked on captured tensors."""
     torch.manual_seed(0)
     m = densenet.random_init(densenet.DenseNet169(), 5)
-    batches = [torch.from_numpy(b) for b in synth.calibration_batches(2, 1, 32, seed=9)]
-    cal = quant.calibrate(m, batches, method="pct", pct=99.0)
+    batches = [torch.from_numpy(b) for b in synth.calibration_batches(3, 1, 32, seed=9)]
+    q = 0.99
+    cal = quant.calibrate(m, batches, method="pct", pct=100 * q)
     cal_max = quant.calibrate(m, batches, method="max")
-    x = torch.cat(batches)
-    a = x.abs().reshape(-1).sort(descending=True).values
-    k = int(np.ceil(0.01 * a.numel()))
-    # in1.0.0 is the conv1 input of the first dense layer = the pool0 output, not x; check the
-    # stem seg (per channel) against the max method's bound and the ordering property instead
-    assert float(cal["in1.0.0"]) <= float(cal_max["in1.0.0"])
-    assert all(p <= q + 1e-12 for p, q in zip(cal["seg0.0"], cal_max["seg0.0"]))
-    assert a[k - 1] > 0
+    layer = m.features.denseblock2.denselayer4
+    seen_in, seen_out = [], []
+    h1 = layer.conv2.register_forward_pre_hook(lambda _m, i: seen_in.append(i[0].detach().clone()))
+    h2 = layer.conv2.register_forward_hook(lambda _m, _i, y: seen_out.append(y.detach().clone()))
+    with torch.no_grad():
+        for x in batches:
+            m(x)
+    h1.remove()
+    h2.remove()
+    a = torch.cat([t.abs().reshape(-1) for t in seen_in]).double().sort(descending=True).values
+    k = int(np.ceil((1 - q) * a.numel()))
+    assert float(cal["in2.1.3"]) == pytest.approx(float(a[k - 1]), rel=1e-6)
+    y = torch.cat([t.abs().transpose(0, 1).reshape(t.shape[1], -1) for t in seen_out], 1).double()
+    kc = int(np.ceil((1 - q) * y.shape[1]))
+    want = y.sort(1, descending=True).values[:, kc - 1].numpy()
+    np.testing.assert_allclose(cal["conv2.1.3"], want, rtol=1e-6)
+    np.testing.assert_allclose(cal_max["conv2.1.3"], y.amax(1).numpy(), rtol=1e-6)
     with pytest.raises(ValueError):
         quant.calibrate(m, batches, method="median")
 
@@ -155,3 +165,26 @@ def test_two_rank_shard_and_gather_gloo(n_studies):
     for _, _, full, tmax in res:
         np.testing.assert_allclose(full, want, rtol=1e-6)
         assert tmax == 2.0
+
+
+def test_bench_work_model_matches_the_per_image_totals():
+    """bench.py's per-launch algorithmic work summed over one 512 px image: 128.1 MB of HBM traffic
+    (activations, every tensor once) and 17.55 GMAC (transitions in the exact full-res integer form)."""
+    import bench
+    blocks = [{"c0": 64, "h": 128, "w": 128, "L": 6}, {"c0": 128, "h": 64, "w": 64, "L": 12},
+              {"c0": 256, "h": 32, "w": 32, "L": 32}, {"c0": 640, "h": 16, "w": 16, "L": 32}]
+    tb = tm = 0
+    for b, blk in enumerate(blocks):
+        for l in range(blk["L"]):
+            by, m = bench.launch_work("conv1", blk, l, 1, 512)
+            tb, tm = tb + by - (blk["c0"] + 32 * l) * 128, tm + m
+            by, m = bench.launch_work("conv2", blk, l, 1, 512)
+            tb, tm = tb + by - 36864, tm + m
+        if b < 3:
+            by, m = bench.launch_work("trans", blk, 0, 1, 512)
+            tb, tm = tb + by, tm + m
+    for kind, blk in (("stem", blocks[0]), ("head", blocks[3])):
+        by, m = bench.launch_work(kind, blk, 0, 1, 512)
+        tb, tm = tb + by, tm + m
+    assert abs(tb / 1e6 - 128.12) < 0.01
+    assert abs(tm / 1e9 - 17.545) < 0.001
