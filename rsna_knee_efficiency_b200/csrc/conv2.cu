@@ -140,6 +140,14 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         const int quad = warp & 3, ch = (warp - 2) >> 2;
         const int p = quad * 32 + lane;                       // pixel within the tile
         const int yl = p / W, x = p - yl * W;
+        const bool has_l = x > 0, has_r = x < W - 1;
+        // the 16 output scales of this channel half, in registers for the whole kernel
+        float sc[16];
+#pragma unroll
+        for (int o = 0; o < 16; ++o) sc[o] = sSc[ch * 16 + o];
+        // the neighbour quads whose edge columns this warp's lanes 0 / 31 need (clamped: unused
+        // when there is none)
+        const int ql = quad > 0 ? quad - 1 : 0, qr = quad < 3 ? quad + 1 : 3;
         for (int t = 0; t < my_tiles; ++t) {
             const int acc = t & 1;
             if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
@@ -153,21 +161,50 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[acc]);
+            // edge columns for the neighbour quads: lane 31's left tap (D[p][0]) and lane 0's right
+            // tap (D[p][2]), as 16-byte stores
             int32_t* xq = xb + ((acc * 2 + ch) * 4) * 32;     // [quad][2][16]
             if (lane == 31)
 #pragma unroll
-                for (int o = 0; o < 16; ++o) xq[quad * 32 + o] = static_cast<int32_t>(d0[o]);
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<uint4*>(xq + quad * 32 + 4 * j) =
+                        make_uint4(d0[4 * j], d0[4 * j + 1], d0[4 * j + 2], d0[4 * j + 3]);
             if (lane == 0)
 #pragma unroll
-                for (int o = 0; o < 16; ++o) xq[quad * 32 + 16 + o] = static_cast<int32_t>(d2[o]);
-            // the four warps of this channel half hand their edge columns over (bounded wait)
+                for (int j = 0; j < 4; ++j)
+                    *reinterpret_cast<uint4*>(xq + quad * 32 + 16 + 4 * j) =
+                        make_uint4(d2[4 * j], d2[4 * j + 1], d2[4 * j + 2], d2[4 * j + 3]);
             __syncwarp();
             if (lane == 0) mbar_arrive(&xbar[acc * 2 + ch]);
+            // in-warp neighbours: all 32 shuffles issued back to back
+            int32_t l[16], r[16];
+#pragma unroll
+            for (int o = 0; o < 16; ++o) {
+                l[o] = __shfl_up_sync(0xffffffffu, static_cast<int32_t>(d0[o]), 1);
+                r[o] = __shfl_down_sync(0xffffffffu, static_cast<int32_t>(d2[o]), 1);
+            }
+            // the four warps of this channel half have published their edges (bounded wait)
             if (!mbar_wait(&xbar[acc * 2 + ch], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            // cross-warp neighbours: uniform (broadcast) 16-byte reads, then per-lane selects
+            const bool at_l = lane == 0, at_r = lane == 31;
+            const bool use_l = has_l && !(at_l && quad == 0), use_r = has_r && !(at_r && quad == 3);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint4 el = *reinterpret_cast<const uint4*>(xq + ql * 32 + 4 * j);
+                const uint4 er = *reinterpret_cast<const uint4*>(xq + qr * 32 + 16 + 4 * j);
+                const int32_t le[4] = {static_cast<int32_t>(el.x), static_cast<int32_t>(el.y),
+                                       static_cast<int32_t>(el.z), static_cast<int32_t>(el.w)};
+                const int32_t re[4] = {static_cast<int32_t>(er.x), static_cast<int32_t>(er.y),
+                                       static_cast<int32_t>(er.z), static_cast<int32_t>(er.w)};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    l[4 * j + k] = use_l ? (at_l ? le[k] : l[4 * j + k]) : 0;
+                    r[4 * j + k] = use_r ? (at_r ? re[k] : r[4 * j + k]) : 0;
+                }
+            }
             const int tile = blockIdx.x + t * gridDim.x;
             const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
             const bool valid = yl < Rt && y0 + yl < H;
-            const bool has_l = x > 0, has_r = x < W - 1;
             uint32_t wd[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -175,14 +212,10 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int o = j * 4 + k;
-                    int32_t l = __shfl_up_sync(0xffffffffu, static_cast<int32_t>(d0[o]), 1);
-                    int32_t r = __shfl_down_sync(0xffffffffu, static_cast<int32_t>(d2[o]), 1);
-                    if (lane == 0) l = quad > 0 ? xq[(quad - 1) * 32 + o] : 0;
-                    if (lane == 31) r = quad < 3 ? xq[(quad + 1) * 32 + 16 + o] : 0;
-                    const int32_t accv = static_cast<int32_t>(d1[o]) + (has_l ? l : 0) + (has_r ? r : 0);
+                    const int32_t accv = static_cast<int32_t>(d1[o]) + l[o] + r[o];
                     const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
                                              : __int2float_rn(accv);
-                    word |= q_s8(f * sSc[ch * 16 + o]) << (8 * k);
+                    word |= q_s8(f * sc[o]) << (8 * k);
                 }
                 wd[j] = word;
             }
