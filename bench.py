@@ -44,7 +44,7 @@ def parse():
     p.add_argument("--steps", type=int, default=40)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--studies", type=int, default=8, help="studies per GPU per step")
+    p.add_argument("--studies", type=int, default=16, help="studies per GPU per step")
     p.add_argument("--pool", type=int, default=0, help="distinct synthetic studies resident per GPU (default: --studies)")
     p.add_argument("--img", type=int, default=512)
     p.add_argument("--flip-tta", action="store_true")

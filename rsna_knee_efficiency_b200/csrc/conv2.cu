@@ -22,6 +22,7 @@ namespace dn8 {
 constexpr int C2_STAGES = 3;
 constexpr int C2_THREADS = 320;
 constexpr int C2_W_BYTES = 36864;            // [dy][cblk][2 halves][96 rows][16 B]
+constexpr int C2_XBUF = 3;                   // edge-exchange buffers (tile t uses t % 3)
 
 static inline int c2_rows_per_tile(int H, int W) {
     int rt = 128 / W;
@@ -37,8 +38,8 @@ static inline size_t c2_stage_bytes(int Rt, int W) {
 }
 size_t conv2_smem_bytes(int H, int W) {
     const int Rt = c2_rows_per_tile(H, W);
-    return 1024 + C2_W_BYTES + C2_STAGES * c2_stage_bytes(Rt, W) + 128 + 2 * 2 * 4 * 2 * 16 * 4 +
-           8 * (2 * C2_STAGES + 9) + 16;
+    return 1024 + C2_W_BYTES + C2_STAGES * c2_stage_bytes(Rt, W) + 128 + C2_XBUF * 2 * 4 * 2 * 16 * 4 +
+           8 * (2 * C2_STAGES + 5 + 2 * C2_XBUF) + 16;
 }
 
 __global__ void __launch_bounds__(C2_THREADS, 1)
@@ -48,13 +49,13 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
     uint8_t* sW = smem;
     uint8_t* sX = smem + C2_W_BYTES;                       // stages, 1024-aligned (36864 = 36 * 1024)
     float* sSc = reinterpret_cast<float*>(sX + C2_STAGES * stage_bytes);
-    int32_t* xb = reinterpret_cast<int32_t*>(sSc + 32);    // [2 acc][2 ch][4 quad][2][16]
-    uint64_t* full = reinterpret_cast<uint64_t*>(xb + 2 * 2 * 4 * 2 * 16);
+    int32_t* xb = reinterpret_cast<int32_t*>(sSc + 32);    // [XBUF][2 ch][4 quad][2][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(xb + C2_XBUF * 2 * 4 * 2 * 16);
     uint64_t* empty = full + C2_STAGES;
     uint64_t* accf = empty + C2_STAGES;
     uint64_t* acce = accf + 2;
-    uint64_t* xbar = acce + 2;                             // [2 acc][2 ch]: neighbour exchange
-    uint64_t* wfull = xbar + 4;
+    uint64_t* xbar = acce + 2;                             // [XBUF][2 ch]: neighbour exchange
+    uint64_t* wfull = xbar + 2 * C2_XBUF;
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(wfull + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
@@ -74,7 +75,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             mbar_init(&accf[k], 1);
             mbar_init(&acce[k], 8);
         }
-        for (int k = 0; k < 4; ++k) mbar_init(&xbar[k], 4);
+        for (int k = 0; k < 2 * C2_XBUF; ++k) mbar_init(&xbar[k], 4);
         mbar_init(&wfull[0], 1);
         *s_abort = 0;
         mbar_fence_init();
@@ -137,23 +138,26 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         __syncwarp();
     } else {
         // ---------------- epilogue ----------------
+        // Software pipeline over two tiles: iteration t loads tile t's accumulator (releasing it to
+        // the MMA at once) and publishes its edge columns, then finishes tile t - 1, whose
+        // neighbours' edges were published an iteration ago. Tile t's edges live in buffer t % 3:
+        // before writing it a warp waits for exchange t - 1, by which every warp of its channel
+        // half has finished tile t - 3 (the buffer's previous reader).
         const int quad = warp & 3, ch = (warp - 2) >> 2;
         const int p = quad * 32 + lane;                       // pixel within the tile
         const int yl = p / W, x = p - yl * W;
         const bool has_l = x > 0, has_r = x < W - 1;
-        // the 16 output scales of this channel half, in registers for the whole kernel
-        float sc[16];
+        const bool at_l = lane == 0, at_r = lane == 31;
+        float sc[16];                                         // this channel half's output scales
 #pragma unroll
         for (int o = 0; o < 16; ++o) sc[o] = sSc[ch * 16 + o];
-        // the neighbour quads whose edge columns this warp's lanes 0 / 31 need (clamped: unused
-        // when there is none)
         const int ql = quad > 0 ? quad - 1 : 0, qr = quad < 3 ? quad + 1 : 3;
-        for (int t = 0; t < my_tiles; ++t) {
+
+        auto load = [&](int t, uint32_t (&d0)[16], uint32_t (&d1)[16], uint32_t (&d2)[16]) -> bool {
             const int acc = t & 1;
-            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) return false;
             tc_fence_after();
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * 128 + ch * 16;
-            uint32_t d0[16], d1[16], d2[16];
             tmem_ld16(taddr, d0);
             tmem_ld16(taddr + 32, d1);
             tmem_ld16(taddr + 64, d2);
@@ -161,67 +165,77 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[acc]);
-            // edge columns for the neighbour quads: lane 31's left tap (D[p][0]) and lane 0's right
-            // tap (D[p][2]), as 16-byte stores
-            int32_t* xq = xb + ((acc * 2 + ch) * 4) * 32;     // [quad][2][16]
-            if (lane == 31)
+            return true;
+        };
+        auto publish = [&](int t, const uint32_t (&d0)[16], const uint32_t (&d2)[16]) {
+            // lane 31's left tap D[p][0] and lane 0's right tap D[p][2] for the neighbour quads
+            int32_t* xq = xb + ((t % C2_XBUF) * 2 + ch) * 4 * 32;      // [quad][2][16]
+            if (at_r)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     *reinterpret_cast<uint4*>(xq + quad * 32 + 4 * j) =
                         make_uint4(d0[4 * j], d0[4 * j + 1], d0[4 * j + 2], d0[4 * j + 3]);
-            if (lane == 0)
+            if (at_l)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     *reinterpret_cast<uint4*>(xq + quad * 32 + 16 + 4 * j) =
                         make_uint4(d2[4 * j], d2[4 * j + 1], d2[4 * j + 2], d2[4 * j + 3]);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&xbar[acc * 2 + ch]);
-            // in-warp neighbours: all 32 shuffles issued back to back
-            int32_t l[16], r[16];
-#pragma unroll
-            for (int o = 0; o < 16; ++o) {
-                l[o] = __shfl_up_sync(0xffffffffu, static_cast<int32_t>(d0[o]), 1);
-                r[o] = __shfl_down_sync(0xffffffffu, static_cast<int32_t>(d2[o]), 1);
-            }
-            // the four warps of this channel half have published their edges (bounded wait)
-            if (!mbar_wait(&xbar[acc * 2 + ch], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
-            // cross-warp neighbours: uniform (broadcast) 16-byte reads, then per-lane selects
-            const bool at_l = lane == 0, at_r = lane == 31;
-            const bool use_l = has_l && !(at_l && quad == 0), use_r = has_r && !(at_r && quad == 3);
+            if (lane == 0) mbar_arrive(&xbar[(t % C2_XBUF) * 2 + ch]);
+        };
+        auto wait_x = [&](int t) -> bool {
+            return mbar_wait(&xbar[(t % C2_XBUF) * 2 + ch], (t / C2_XBUF) & 1, a.err, s_abort, ERR_WAIT_ACC);
+        };
+        // out[p] = D[p-1][0] + D[p][1] + D[p+1][2] (zero outside the row), requantised (exchange t done)
+        auto finish = [&](int t, const uint32_t (&d0)[16], const uint32_t (&d1)[16], const uint32_t (&d2)[16]) {
+            const int32_t* xq = xb + ((t % C2_XBUF) * 2 + ch) * 4 * 32;
+            uint32_t wd[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const uint4 el = *reinterpret_cast<const uint4*>(xq + ql * 32 + 4 * j);
                 const uint4 er = *reinterpret_cast<const uint4*>(xq + qr * 32 + 16 + 4 * j);
-                const int32_t le[4] = {static_cast<int32_t>(el.x), static_cast<int32_t>(el.y),
-                                       static_cast<int32_t>(el.z), static_cast<int32_t>(el.w)};
-                const int32_t re[4] = {static_cast<int32_t>(er.x), static_cast<int32_t>(er.y),
-                                       static_cast<int32_t>(er.z), static_cast<int32_t>(er.w)};
+                const uint32_t le[4] = {el.x, el.y, el.z, el.w};
+                const uint32_t re[4] = {er.x, er.y, er.z, er.w};
+                uint32_t q[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    l[4 * j + k] = use_l ? (at_l ? le[k] : l[4 * j + k]) : 0;
-                    r[4 * j + k] = use_r ? (at_r ? re[k] : r[4 * j + k]) : 0;
+                    const int o = 4 * j + k;
+                    const uint32_t l = __shfl_up_sync(0xffffffffu, d0[o], 1);
+                    const uint32_t r = __shfl_down_sync(0xffffffffu, d2[o], 1);
+                    const int32_t lv = has_l ? static_cast<int32_t>(at_l ? le[k] : l) : 0;
+                    const int32_t rv = has_r ? static_cast<int32_t>(at_r ? re[k] : r) : 0;
+                    const int32_t accv = static_cast<int32_t>(d1[o]) + lv + rv;
+                    const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
+                                             : __int2float_rn(accv);
+                    // rint(clamp(f sc, +-127)) as the low byte of (clamped + 1.5 * 2^23)
+                    q[k] = __float_as_uint(fminf(fmaxf(f * sc[o], -127.0f), 127.0f) + 12582912.0f);
                 }
+                wd[j] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
             }
             const int tile = blockIdx.x + t * gridDim.x;
             const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
-            const bool valid = yl < Rt && y0 + yl < H;
-            uint32_t wd[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t word = 0;
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int o = j * 4 + k;
-                    const int32_t accv = static_cast<int32_t>(d1[o]) + l[o] + r[o];
-                    const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
-                                             : __int2float_rn(accv);
-                    word |= q_s8(f * sc[o]) << (8 * k);
-                }
-                wd[j] = word;
-            }
-            if (valid) {
+            if (yl < Rt && y0 + yl < H) {
                 int8_t* dst = a.out + ((static_cast<size_t>(n) * H + y0 + yl) * W + x) * 32 + ch * 16;
                 *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+        };
+        auto step = [&](int t, uint32_t (&c0)[16], uint32_t (&c1)[16], uint32_t (&c2)[16],
+                        const uint32_t (&p0)[16], const uint32_t (&p1)[16], const uint32_t (&p2)[16]) -> bool {
+            if (!load(t, c0, c1, c2)) return false;
+            if (t > 0 && !wait_x(t - 1)) return false;
+            publish(t, c0, c2);
+            if (t > 0) finish(t - 1, p0, p1, p2);
+            return true;
+        };
+        uint32_t a0[16], a1[16], a2[16], b0[16], b1[16], b2[16];
+        bool ok = true;
+        for (int t = 0; t < my_tiles && ok; ++t)
+            ok = (t & 1) ? step(t, b0, b1, b2, a0, a1, a2) : step(t, a0, a1, a2, b0, b1, b2);
+        if (ok && my_tiles > 0) {
+            const int t = my_tiles - 1;
+            if (wait_x(t)) {
+                if (t & 1) finish(t, b0, b1, b2);
+                else finish(t, a0, a1, a2);
             }
         }
     }

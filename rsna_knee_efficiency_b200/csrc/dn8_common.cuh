@@ -122,6 +122,13 @@ DN8_DEV void umma_u8s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t
                  "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
                  ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M = 128 rows, K = 32 bytes) in 8 consecutive TMEM columns,
+// row m in lane m, bytes 4c..4c+3 of the row in column c.
+DN8_DEV void umma_u8s8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
 // Arrives once on `bar` when every tcgen05 operation issued so far by this thread has completed.
 DN8_DEV void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"

@@ -34,12 +34,18 @@ constexpr int SMEM_BUDGET = 225 * 1024;
 
 // KSTEP K groups of KSUB sub-tiles per stage (KSTEP * KSUB = 4 units); SR raw slots, SA operand slots
 template <bool TRANS> struct GemmCfg;
+// conv1 keeps its A operands in TMEM (columns 256..511 behind the two 128-column accumulators:
+// SA = 8 stages of 4 units x 8 columns); the transition (NC up to 256 accumulator columns) keeps
+// them in shared memory.
 template <> struct GemmCfg<false> {                // conv1
-    static constexpr int KSUB = 1, KSTEP = 4, SR = 4, SA = 4;
+    static constexpr int KSUB = 1, KSTEP = 4, SR = 4, SA = 8;
+    static constexpr bool TMEM_A = true;
 };
 template <> struct GemmCfg<true> {                 // transition
     static constexpr int KSUB = 4, KSTEP = 1, SR = 4, SA = 4;
+    static constexpr bool TMEM_A = false;
 };
+constexpr uint32_t TMEM_A_COL = 256;               // conv1: first TMEM column of the A stages
 constexpr int UNITS = 4;
 
 struct GemmArgs {
@@ -72,7 +78,8 @@ DN8_DEV void trans_span(int m0, int cnt, int HW, int W, int* first, int* end) {
 static size_t gemm_layout(bool trans, int G, int nc, int nchunks, int raw_bytes, int* sb, int* resident) {
     const int sr = trans ? GemmCfg<true>::SR : GemmCfg<false>::SR, sa = trans ? GemmCfg<true>::SA : GemmCfg<false>::SA;
     const int kstep = trans ? GemmCfg<true>::KSTEP : GemmCfg<false>::KSTEP;
-    const size_t fixed = static_cast<size_t>(sr) * raw_bytes + static_cast<size_t>(sa) * UNITS * 4096;
+    const size_t a_smem = trans ? static_cast<size_t>(sa) * UNITS * 4096 : 0;     // conv1: A in TMEM
+    const size_t fixed = static_cast<size_t>(sr) * raw_bytes + a_smem;
     const size_t misc = 1024 + static_cast<size_t>(G) * 256 + static_cast<size_t>(trans ? 640 : 128) * 8 + 8 * 96 + 64;
     const size_t btile = static_cast<size_t>(nc) * 32;
     if (nchunks == 1 && fixed + misc + btile * G <= SMEM_BUDGET) {
@@ -97,9 +104,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int NC = a.nc, G = a.G, G0 = a.G0, HW = a.HW, rows = a.rows;
     const int btile = NC * 32, RB = a.raw_bytes;
+    constexpr bool TMEM_A = Cfg::TMEM_A;
     uint8_t* sR = smem;                                          // [SR][RB] raw store bytes
-    uint8_t* sA = sR + SR * RB;                                  // [SA][KSUB][128][32] swizzled
-    uint8_t* sB = sA + SA * ASTAGE;                              // weights
+    uint8_t* sA = sR + SR * RB;                                  // [SA][KSUB][128][32] swizzled (transition)
+    uint8_t* sB = sA + (TMEM_A ? 0 : SA * ASTAGE);               // weights
     const int bstage = KSTEP * btile;                            // weight bytes of a streamed stage
     uint8_t* sTab = sB + (a.b_resident ? static_cast<size_t>(G) * btile : static_cast<size_t>(a.sb) * bstage);
     float2* sGd = reinterpret_cast<float2*>(sTab + G * 256);
@@ -120,7 +128,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     const int my_tiles = static_cast<int>(blockIdx.x) < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int NS = (G + KSTEP - 1) / KSTEP;                     // stages per tile
     const int T = my_tiles * NS;
-    const uint32_t tcols = NC > 128 ? 512u : 256u;
+    const uint32_t tcols = (NC > 128 || TMEM_A) ? 512u : 256u;
     const size_t gstride = static_cast<size_t>(a.N) * HW * 32;   // one store group
 
     if (threadIdx.x == 0) {
@@ -210,9 +218,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     for (int x = 0; x < UNITS; ++x) {
                         // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
                         if (TRANS || x < gc) {
-                            const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
                             const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
-                            umma_u8s8(tmem + acc * NC, ad, bd, idesc, 1u);   // accumulators start at MAGIC
+                            if constexpr (TMEM_A) {
+                                umma_u8s8_ts(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
+                                             idesc, 1u);                         // accumulators start at MAGIC
+                            } else {
+                                const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
+                                umma_u8s8(tmem + acc * NC, ad, bd, idesc, 1u);
+                            }
                         }
                     }
                     umma_commit(&emptyA[s]);
@@ -284,6 +297,73 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             }
         }
         __syncwarp();
+    } else if (warp <= 10 && TMEM_A) {
+        // ---------------- prologue, A into TMEM (conv1) ----------------
+        // Warp w writes TMEM lanes 32 (w % 4) .. + 31, so the four warps of one lane quadrant each
+        // take a quarter of the stage's rows: row r = 32 q + lane, all 4 units (K groups) of the
+        // stage; the two warps of a quadrant alternate stages. The 32 raw bytes of a row are read
+        // half-swapped on odd row quads so that a warp's 16-byte reads hit all 32 banks.
+        const int q = warp & 3, kk = (warp - 3) >> 2;
+        const int r = q * 32 + lane;
+        const int sw = (r >> 2) & 1;
+        const uint32_t tlane = static_cast<uint32_t>(q * 32) << 16;
+        for (int i = kk; i < T; i += 2) {
+            const int s = i % SR, sa = i % SA;
+            const int t = i / NS, j = i - t * NS;
+            const int gc = min(KSTEP, G - j * KSTEP);
+            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
+            uint4 lo[UNITS], hi[UNITS];
+#pragma unroll
+            for (int x = 0; x < UNITS; ++x) {
+                if (x < gc) {
+                    const uint8_t* src = sR + s * RB + x * 4096 + r * 32;
+                    const uint4 v0 = *reinterpret_cast<const uint4*>(src + sw * 16);
+                    const uint4 v1 = *reinterpret_cast<const uint4*>(src + (sw ^ 1) * 16);
+                    lo[x] = sw ? v1 : v0;
+                    hi[x] = sw ? v0 : v1;
+                } else {
+                    lo[x] = make_uint4(0, 0, 0, 0);
+                    hi[x] = lo[x];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&freeR[s]);
+            uint32_t res[UNITS * 8];
+#pragma unroll
+            for (int x = 0; x < UNITS; ++x) {
+                const int g = j * KSTEP + (x < gc ? x : 0);
+                if (F16) {
+                    const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128);   // 32 channels
+                    const uint4 t0 = tb[0], t1 = tb[1], t2 = tb[2], t3 = tb[3];
+                    const uint4 t4 = tb[4], t5 = tb[5], t6 = tb[6], t7 = tb[7];
+                    res[8 * x + 0] = prologue_f16x4(lo[x].x, t0.x, t0.y, t0.z, t0.w);
+                    res[8 * x + 1] = prologue_f16x4(lo[x].y, t1.x, t1.y, t1.z, t1.w);
+                    res[8 * x + 2] = prologue_f16x4(lo[x].z, t2.x, t2.y, t2.z, t2.w);
+                    res[8 * x + 3] = prologue_f16x4(lo[x].w, t3.x, t3.y, t3.z, t3.w);
+                    res[8 * x + 4] = prologue_f16x4(hi[x].x, t4.x, t4.y, t4.z, t4.w);
+                    res[8 * x + 5] = prologue_f16x4(hi[x].y, t5.x, t5.y, t5.z, t5.w);
+                    res[8 * x + 6] = prologue_f16x4(hi[x].z, t6.x, t6.y, t6.z, t6.w);
+                    res[8 * x + 7] = prologue_f16x4(hi[x].w, t7.x, t7.y, t7.z, t7.w);
+                } else {
+                    const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32;
+                    res[8 * x + 0] = prologue_f32x4(lo[x].x, tb);
+                    res[8 * x + 1] = prologue_f32x4(lo[x].y, tb + 4);
+                    res[8 * x + 2] = prologue_f32x4(lo[x].z, tb + 8);
+                    res[8 * x + 3] = prologue_f32x4(lo[x].w, tb + 12);
+                    res[8 * x + 4] = prologue_f32x4(hi[x].x, tb + 16);
+                    res[8 * x + 5] = prologue_f32x4(hi[x].y, tb + 20);
+                    res[8 * x + 6] = prologue_f32x4(hi[x].z, tb + 24);
+                    res[8 * x + 7] = prologue_f32x4(hi[x].w, tb + 28);
+                }
+            }
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+            tc_fence_after();
+            tmem_st32(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8), res);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&fullA[sa]);
+        }
     } else if (warp <= 10) {
         // ---------------- prologue ----------------
         // One warp owns a whole unit (128 rows x 32 B = 256 chunks of 16 B; chunk c = jj * 32 + lane is
