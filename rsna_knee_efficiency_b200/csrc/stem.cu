@@ -12,17 +12,19 @@
 // A CTA walks bands of BP pooled rows of one image; for every conv row of the band (2 BP + 1, the
 // first one is the halo shared with the band above):
 //   warps 1-4  load the two new input rows (all 3 channels) into a 16-row ring (column c at byte
-//              c + 4, four zero bytes either side), build the im2col tile of the conv row
-//              (ceil(CW / 128) M-tiles x 6 K steps, 32B-swizzled), double-buffered;
+//              c + 4, four zero bytes either side; the next conv row's loads are issued before this
+//              row's im2col), build the im2col tile of the conv row (ceil(CW / 128) M-tiles x 6 K
+//              steps, 32B-swizzled, pixel u of a tile in row u / 2 or 64 + u / 2), double-buffered;
 //   warp 0     TMEM owner / MMA issuer: M128 N64 K32 MMAs into one of two TMEM accumulators;
-//   warps 5-8  requantise into a 3-row ring of conv outputs; after every odd conv row 2 py + 1 they
-//              max-pool pooled row py (conv rows 2py-1 .. 2py+1) and write it out.
+//   warps 5-12 (a lane quadrant x a 32-channel half each) requantise into a 3-row ring of conv
+//              outputs; after every odd conv row 2 py + 1 they max-pool pooled row py (conv rows
+//              2py-1 .. 2py+1) and write it out.
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
 namespace dn8 {
 
-constexpr int ST_THREADS = 288;
+constexpr int ST_THREADS = 416;          // warp 0 MMA, 1-4 rows + im2col, 5-12 epilogue
 constexpr int ST_BP = 16;                 // pooled rows per band
 constexpr int ST_RING = 16;               // input row ring
 constexpr int ST_KSTEPS = 6;
@@ -85,10 +87,10 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             mbar_init(&fullA[k], 4);
             mbar_init(&emptyA[k], 1);
             mbar_init(&accf[k], 1);
-            mbar_init(&acce[k], 4);
+            mbar_init(&acce[k], 8);
             mbar_init(&ringrdy[k], 4);
-            mbar_init(&written[k], 4);
-            mbar_init(&done[k], 4);
+            mbar_init(&written[k], 8);
+            mbar_init(&done[k], 8);
         }
         mbar_init(&wfull[0], 1);
         *s_abort = 0;
@@ -114,11 +116,10 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         uint32_t arm[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
-        const int quad = warp & 3;
+        const int quad = warp & 3, hc = (warp - 5) >> 2;
         for (int acc = 0; acc < 2; ++acc)
             for (int m = 0; m < MT; ++m)
-                for (int cb = 0; cb < 64; cb += 32)
-                    tmem_st32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * 128 + m * 64 + cb, arm);
+                tmem_st32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * 128 + m * 64 + hc * 32, arm);
         tmem_wait_st();
     }
     tc_fence_before();
@@ -169,51 +170,49 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     } else if (warp <= 4) {
         // ---------------- input rows + im2col ----------------
         const int pt = threadIdx.x - 32;                  // 0..127
-        // load input row y (all 3 channels) of image n into ring slot y % ST_RING
-        auto load_row = [&](int n, int y) {
-            uint8_t* dst = sRing + (y & (ST_RING - 1)) * 3 * RB;
-            const bool inside = y >= 0 && y < H;
-            const int flip = a.flags != nullptr ? (a.flags[n] & 1) : 0;
+        // Input row y (all 3 channels) of image n: fetched into registers (one word of 4 pixels,
+        // or four fp16 pixels, per channel and thread; the loads of a row are independent), then
+        // put into ring slot y % ST_RING (column c at byte c + 4, flipped if asked).
+        int planes[3] = {0, 0, 0};                        // uint8 planes of the task's image
+        auto fetch = [&](int n, int y, uint2 (&rv)[3]) {
+            const bool inside = y >= 0 && y < H && pt < W / 4;
+#pragma unroll
             for (int ch = 0; ch < 3; ++ch) {
-                uint8_t* drow = dst + ch * RB + 4;
-                if (a.x_u8) {
-                    const uint8_t* src = nullptr;
-                    if (inside) {
-                        const int plane = a.src[n * 4 + ch];
-                        src = static_cast<const uint8_t*>(a.x) + (static_cast<size_t>(plane) * H + y) * W;
-                    }
-                    for (int c4 = pt; c4 < W / 4; c4 += 128) {
-                        uint32_t v = inside ? __ldg(reinterpret_cast<const uint32_t*>(src) + c4) : 0u;
-                        int col = 4 * c4;
-                        if (flip) {
-                            v = __byte_perm(v, 0, 0x0123);
-                            col = W - 4 - col;
-                        }
-                        *reinterpret_cast<uint32_t*>(drow + col) = v;
-                    }
-                } else {
-                    const uint16_t* src = inside ? static_cast<const uint16_t*>(a.x) + ((static_cast<size_t>(n) * 3 + ch) * H + y) * W
-                                                 : nullptr;
-                    for (int c4 = pt; c4 < W / 4; c4 += 128) {
-                        uint32_t v = 0u;
-                        if (inside) {
-                            const uint2 hv = __ldg(reinterpret_cast<const uint2*>(src) + c4);
-                            v = u8_of_f16x2(hv.x) | (u8_of_f16x2(hv.y) << 16);
-                        }
-                        int col = 4 * c4;
-                        if (flip) {
-                            v = __byte_perm(v, 0, 0x0123);
-                            col = W - 4 - col;
-                        }
-                        *reinterpret_cast<uint32_t*>(drow + col) = v;
+                rv[ch] = make_uint2(0u, 0u);
+                if (inside) {
+                    if (a.x_u8) {
+                        rv[ch].x = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.x) +
+                                                                             (static_cast<size_t>(planes[ch]) * H + y) * W) + pt);
+                    } else {
+                        rv[ch] = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(a.x) +
+                                                                      ((static_cast<size_t>(n) * 3 + ch) * H + y) * W) + pt);
                     }
                 }
             }
         };
+        auto put = [&](int n, int y, const uint2 (&rv)[3]) {
+            if (pt >= W / 4) return;
+            uint8_t* dst = sRing + (y & (ST_RING - 1)) * 3 * RB + 4;
+            const int flip = a.flags != nullptr ? (a.flags[n] & 1) : 0;
+#pragma unroll
+            for (int ch = 0; ch < 3; ++ch) {
+                uint32_t v = a.x_u8 ? rv[ch].x : (u8_of_f16x2(rv[ch].x) | (u8_of_f16x2(rv[ch].y) << 16));
+                int col = 4 * pt;
+                if (flip) {
+                    v = __byte_perm(v, 0, 0x0123);
+                    col = W - 4 - col;
+                }
+                *reinterpret_cast<uint32_t*>(dst + ch * RB + col) = v;
+            }
+        };
         int i = 0;
+        uint2 pre0[3], pre1[3];                           // the next conv row's two input rows
         for (int t = 0; t < my_tasks; ++t) {
             int n, py0, cr0, nrows;
             task_rows(t, n, py0, cr0, nrows);
+            if (a.x_u8)
+#pragma unroll
+                for (int ch = 0; ch < 3; ++ch) planes[ch] = a.src[n * 4 + ch];
             bool ok_run = true;
             for (int r = 0; r < nrows; ++r, ++i) {
                 const int cr = cr0 + r;
@@ -226,25 +225,39 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         ok_run = false;
                         break;
                     }
-                    for (int y = 2 * cr - 3; y <= 2 * cr + 3; ++y) load_row(n, y);
+                    for (int k = 0; k < 7; k += 2) {              // two rows' loads in flight at a time
+                        fetch(n, 2 * cr - 3 + k, pre0);
+                        if (k + 1 < 7) fetch(n, 2 * cr - 2 + k, pre1);
+                        put(n, 2 * cr - 3 + k, pre0);
+                        if (k + 1 < 7) put(n, 2 * cr - 2 + k, pre1);
+                    }
                 } else {
-                    load_row(n, 2 * cr + 2);
-                    load_row(n, 2 * cr + 3);
+                    put(n, 2 * cr + 2, pre0);
+                    put(n, 2 * cr + 3, pre1);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ringrdy[i & 1]);
                 if (!mbar_wait(&ringrdy[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                // the next conv row's input rows load while this row's im2col tile is built
+                if (r + 1 < nrows) {
+                    fetch(n, 2 * cr + 4, pre0);
+                    fetch(n, 2 * cr + 5, pre1);
+                }
                 const int b = i & 1;
                 if (!mbar_wait(&emptyA[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
-                for (int m = 0; m < MT; ++m) {
-                    const int cx = min(m * 128 + pt, CW - 1);     // rows past the conv width: junk
-                    const int s2 = 2 * cx;                        // slot start byte in a ring row
-                    const int wb = s2 & ~3, sh = (s2 & 3) * 8;
+                // im2col of the conv row: thread pt builds conv pixels u = 2p and 2p + 1 (p = pt % 64) of
+                // M-tile pt / 64, as tile rows p and p + 64 (the epilogue maps lane L back to pixel
+                // 2L or 2(L - 64) + 1), so a warp's 16-byte stores cover 32 consecutive rows; the two
+                // 8-byte windows start at ring bytes 2 cx and 2 cx + 2, so three aligned words per slot
+                // serve both
+                if (pt < MT * 64) {
+                    const int m = pt >> 6, r0 = pt & 63;
+                    const int wb = 2 * min(m * 128 + 2 * r0, CW - 2);  // pixels past the conv width: junk rows
                     uint8_t* tile = sA + (b * MT + m) * ST_KSTEPS * 4096;
-                    const int r32 = pt * 32, swz = ((pt >> 2) & 1) << 4;
+                    const int swz0 = ((r0 >> 2) & 1) << 4, swz1 = swz0;
 #pragma unroll
                     for (int kk = 0; kk < ST_KSTEPS; ++kk) {
-                        uint32_t wv[8];
+                        uint32_t w0v[8], w1v[8];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const int sl = kk * 4 + e;                // slot (ch, ky)
@@ -252,18 +265,23 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                                 const int ch = sl / 7, ky = sl - ch * 7;
                                 const int y = 2 * cr + ky - 3;
                                 const uint8_t* row = sRing + ((y & (ST_RING - 1)) * 3 + ch) * RB + wb;
-                                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(row);
-                                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(row + 4);
-                                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(row + 8);
-                                wv[2 * e] = __funnelshift_r(w0, w1, sh);
-                                wv[2 * e + 1] = __funnelshift_r(w1, w2, sh);
+                                const uint32_t u0 = *reinterpret_cast<const uint32_t*>(row);
+                                const uint32_t u1 = *reinterpret_cast<const uint32_t*>(row + 4);
+                                const uint32_t u2 = *reinterpret_cast<const uint32_t*>(row + 8);
+                                w0v[2 * e] = u0;
+                                w0v[2 * e + 1] = u1;
+                                w1v[2 * e] = __funnelshift_r(u0, u1, 16);
+                                w1v[2 * e + 1] = __funnelshift_r(u1, u2, 16);
                             } else {
-                                wv[2 * e] = wv[2 * e + 1] = 0u;
+                                w0v[2 * e] = w0v[2 * e + 1] = w1v[2 * e] = w1v[2 * e + 1] = 0u;
                             }
                         }
-                        uint8_t* d = tile + kk * 4096 + r32;
-                        *reinterpret_cast<uint4*>(d + swz) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                        *reinterpret_cast<uint4*>(d + (swz ^ 16)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+                        uint8_t* d0 = tile + kk * 4096 + r0 * 32;
+                        *reinterpret_cast<uint4*>(d0 + swz0) = make_uint4(w0v[0], w0v[1], w0v[2], w0v[3]);
+                        *reinterpret_cast<uint4*>(d0 + (swz0 ^ 16)) = make_uint4(w0v[4], w0v[5], w0v[6], w0v[7]);
+                        uint8_t* d1 = d0 + 64 * 32;
+                        *reinterpret_cast<uint4*>(d1 + swz1) = make_uint4(w1v[0], w1v[1], w1v[2], w1v[3]);
+                        *reinterpret_cast<uint4*>(d1 + (swz1 ^ 16)) = make_uint4(w1v[4], w1v[5], w1v[6], w1v[7]);
                     }
                 }
                 fence_async_smem();
@@ -274,8 +292,15 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         }
     } else {
         // ---------------- epilogue: requantise, ring, max-pool ----------------
-        const int quad = warp & 3;
-        const int et = threadIdx.x - 160;                 // 0..127
+        // 8 warps: warp w reads TMEM lanes 32 (w % 4) .. + 31 (conv pixels) and channel half hc;
+        // the pooling splits the pooled pixels x channel halves (= the two output groups) likewise.
+        const int quad = warp & 3, hc = (warp - 5) >> 2;
+        const int et = threadIdx.x - 160;                 // 0..255
+        const int pxh = et & 1, px0 = et >> 1;            // pooling: channel half, first pooled pixel
+        const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
+        uint32_t arm[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
         int i = 0;
         for (int t = 0; t < my_tasks; ++t) {
             int n, py0, cr0, nrows;
@@ -290,39 +315,46 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 if (!mbar_wait(&accf[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
                 tc_fence_after();
                 for (int m = 0; m < MT; ++m) {
-                    const int cx = m * 128 + quad * 32 + lane;
-                    uint32_t wd[16];
+                    const int row = quad * 32 + lane;              // tile row -> conv pixel (see im2col)
+                    const int cx = m * 128 + (row < 64 ? 2 * row : 2 * (row - 64) + 1);
+                    uint32_t v[32];
+                    const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 128 + m * 64 + hc * 32;
+                    tmem_ld32(taddr, v);
+                    tmem_wait_ld();
+                    tmem_st32(taddr, arm);
+                    uint32_t wd[8];
 #pragma unroll
-                    for (int cb = 0; cb < 2; ++cb) {
-                        uint32_t v[32];
-                        const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 128 + m * 64 + cb * 32;
-                        tmem_ld32(taddr, v);
-                        tmem_wait_ld();
-                        uint32_t arm[32];
+                    for (int j = 0; j < 8; ++j) {
+                        // k, c of the 4 channels (broadcast reads); fmaf pairwise in f32x2
+                        const float4 k4 = *reinterpret_cast<const float4*>(sKC + hc * 32 + 4 * j);
+                        const float4 c4 = *reinterpret_cast<const float4*>(sKC + 64 + hc * 32 + 4 * j);
+                        float f[4];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
-                        tmem_st32(taddr, arm);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            uint32_t bq[4];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const int o = cb * 32 + 4 * j + e;
-                                const float f = fast_cvt ? __uint_as_float(v[4 * j + e]) - ACC_MAGIC_F
-                                                         : __int2float_rn(static_cast<int32_t>(v[4 * j + e] - ACC_MAGIC));
-                                const float tq = fminf(fmaxf(fmaf(f, sKC[o], sKC[64 + o]), 0.0f), 127.0f);
-                                bq[e] = __float_as_uint(tq + 12582912.0f);
+                        for (int e = 0; e < 4; e += 2) {
+                            if (fast_cvt) {
+                                f2_unpack(f2_add(f2_pack(__uint_as_float(v[4 * j + e]), __uint_as_float(v[4 * j + e + 1])),
+                                                 f2_pack(-ACC_MAGIC_F, -ACC_MAGIC_F)), f[e], f[e + 1]);
+                            } else {
+                                f[e] = __int2float_rn(static_cast<int32_t>(v[4 * j + e] - ACC_MAGIC));
+                                f[e + 1] = __int2float_rn(static_cast<int32_t>(v[4 * j + e + 1] - ACC_MAGIC));
                             }
-                            wd[cb * 8 + j] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040),
-                                                         __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
                         }
+                        float tq[4];
+                        f2_unpack(f2_fma(f2_pack(f[0], f[1]), f2_pack(k4.x, k4.y), f2_pack(c4.x, c4.y)), tq[0], tq[1]);
+                        f2_unpack(f2_fma(f2_pack(f[2], f[3]), f2_pack(k4.z, k4.w), f2_pack(c4.z, c4.w)), tq[2], tq[3]);
+                        uint32_t bq[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            bq[e] = __float_as_uint(fminf(fmaxf(tq[e], 0.0f), 127.0f) + 12582912.0f);
+                        wd[j] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
                     }
                     if (cx < CW) {
-                        // conv ring [3][MT * 128][64 B]; chunk j of pixel p at (j ^ (p & 3)) spreads the banks
-                        uint8_t* cp = sC + (static_cast<size_t>(slot) * MT * 128 + cx) * 64;
+                        // conv ring [3][MT][128 tile rows][64 B], by tile row; chunk j of row r at
+                        // (j ^ (r & 3)) spreads the banks
+                        uint8_t* cp = sC + (static_cast<size_t>(slot) * MT * 128 + m * 128 + row) * 64;
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            *reinterpret_cast<uint4*>(cp + ((j ^ (cx & 3)) << 4)) =
+                        for (int j = 0; j < 2; ++j)
+                            *reinterpret_cast<uint4*>(cp + (((2 * hc + j) ^ (row & 3)) << 4)) =
                                 make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]);
                     }
                 }
@@ -337,21 +369,25 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 const int py = (cr - 1) >> 1;
                 if ((cr & 1) == 1 && py >= py0) {
                     if (!mbar_wait(&written[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
-                    for (int px = et; px < PW; px += 128) {
-                        uint32_t mx[16];
+                    for (int px = px0; px < PW; px += 128) {
+                        uint32_t mx[8];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) mx[j] = 0u;
+                        for (int j = 0; j < 8; ++j) mx[j] = 0u;
+#pragma unroll
                         for (int dy = -1; dy <= 1; ++dy) {
                             const int cyy = 2 * py + dy;
                             if (cyy < 0 || cyy >= CH) continue;
                             const uint8_t* rowp = sC + static_cast<size_t>(cyy % 3) * MT * 128 * 64;
+#pragma unroll
                             for (int dx = -1; dx <= 1; ++dx) {
                                 const int cxx = 2 * px + dx;
                                 if (cxx < 0 || cxx >= CW) continue;
-                                const uint8_t* pp = rowp + cxx * 64;
+                                const int u = cxx & 127;
+                                const int trow = (u & 1) ? 64 + (u >> 1) : (u >> 1);
+                                const uint8_t* pp = rowp + ((cxx >> 7) * 128 + trow) * 64;
 #pragma unroll
-                                for (int j = 0; j < 4; ++j) {
-                                    const uint4 q = *reinterpret_cast<const uint4*>(pp + ((j ^ (cxx & 3)) << 4));
+                                for (int j = 0; j < 2; ++j) {
+                                    const uint4 q = *reinterpret_cast<const uint4*>(pp + (((2 * pxh + j) ^ (trow & 3)) << 4));
                                     mx[4 * j] = __vmaxu4(mx[4 * j], q.x);
                                     mx[4 * j + 1] = __vmaxu4(mx[4 * j + 1], q.y);
                                     mx[4 * j + 2] = __vmaxu4(mx[4 * j + 2], q.z);
@@ -359,14 +395,11 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                                 }
                             }
                         }
-                        // block 1 input, group-major [2][N][PH * PW][32]
+                        // block 1 input, group-major [2][N][PH * PW][32]: this half is group pxh
                         const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
-                        const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
-                        int8_t* o = a.out + pix * 32;
+                        int8_t* o = a.out + pxh * gstride + pix * 32;
                         *reinterpret_cast<uint4*>(o) = make_uint4(mx[0], mx[1], mx[2], mx[3]);
                         *reinterpret_cast<uint4*>(o + 16) = make_uint4(mx[4], mx[5], mx[6], mx[7]);
-                        *reinterpret_cast<uint4*>(o + gstride) = make_uint4(mx[8], mx[9], mx[10], mx[11]);
-                        *reinterpret_cast<uint4*>(o + gstride + 16) = make_uint4(mx[12], mx[13], mx[14], mx[15]);
                     }
                 }
                 __syncwarp();
