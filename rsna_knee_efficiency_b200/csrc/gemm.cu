@@ -312,53 +312,51 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int t = i / NS, j = i - t * NS;
             const int gc = min(KSTEP, G - j * KSTEP);
             if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
-            uint4 lo[UNITS], hi[UNITS];
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+            tc_fence_after();
+            // one unit (K group) at a time: 32 raw bytes -> 8 prologue words -> 8 TMEM columns
 #pragma unroll
             for (int x = 0; x < UNITS; ++x) {
-                if (x < gc) {
-                    const uint8_t* src = sR + s * RB + x * 4096 + r * 32;
-                    const uint4 v0 = *reinterpret_cast<const uint4*>(src + sw * 16);
-                    const uint4 v1 = *reinterpret_cast<const uint4*>(src + (sw ^ 1) * 16);
-                    lo[x] = sw ? v1 : v0;
-                    hi[x] = sw ? v0 : v1;
+                if (x >= gc) break;
+                const int g = j * KSTEP + x;
+                const uint8_t* src = sR + s * RB + x * 4096 + r * 32;
+                const uint4 v0 = *reinterpret_cast<const uint4*>(src + sw * 16);
+                const uint4 v1 = *reinterpret_cast<const uint4*>(src + (sw ^ 1) * 16);
+                const uint4 lo = sw ? v1 : v0, hi = sw ? v0 : v1;
+                uint32_t res[8];
+                if (F16) {
+                    const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128);   // 32 channels
+                    uint4 tt = tb[0];
+                    res[0] = prologue_f16x4(lo.x, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[1];
+                    res[1] = prologue_f16x4(lo.y, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[2];
+                    res[2] = prologue_f16x4(lo.z, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[3];
+                    res[3] = prologue_f16x4(lo.w, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[4];
+                    res[4] = prologue_f16x4(hi.x, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[5];
+                    res[5] = prologue_f16x4(hi.y, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[6];
+                    res[6] = prologue_f16x4(hi.z, tt.x, tt.y, tt.z, tt.w);
+                    tt = tb[7];
+                    res[7] = prologue_f16x4(hi.w, tt.x, tt.y, tt.z, tt.w);
                 } else {
-                    lo[x] = make_uint4(0, 0, 0, 0);
-                    hi[x] = lo[x];
+                    const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32;
+                    res[0] = prologue_f32x4(lo.x, tb);
+                    res[1] = prologue_f32x4(lo.y, tb + 4);
+                    res[2] = prologue_f32x4(lo.z, tb + 8);
+                    res[3] = prologue_f32x4(lo.w, tb + 12);
+                    res[4] = prologue_f32x4(hi.x, tb + 16);
+                    res[5] = prologue_f32x4(hi.y, tb + 20);
+                    res[6] = prologue_f32x4(hi.z, tb + 24);
+                    res[7] = prologue_f32x4(hi.w, tb + 28);
                 }
+                tmem_st8(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8) + x * 8, res);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&freeR[s]);
-            uint32_t res[UNITS * 8];
-#pragma unroll
-            for (int x = 0; x < UNITS; ++x) {
-                const int g = j * KSTEP + (x < gc ? x : 0);
-                if (F16) {
-                    const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128);   // 32 channels
-                    const uint4 t0 = tb[0], t1 = tb[1], t2 = tb[2], t3 = tb[3];
-                    const uint4 t4 = tb[4], t5 = tb[5], t6 = tb[6], t7 = tb[7];
-                    res[8 * x + 0] = prologue_f16x4(lo[x].x, t0.x, t0.y, t0.z, t0.w);
-                    res[8 * x + 1] = prologue_f16x4(lo[x].y, t1.x, t1.y, t1.z, t1.w);
-                    res[8 * x + 2] = prologue_f16x4(lo[x].z, t2.x, t2.y, t2.z, t2.w);
-                    res[8 * x + 3] = prologue_f16x4(lo[x].w, t3.x, t3.y, t3.z, t3.w);
-                    res[8 * x + 4] = prologue_f16x4(hi[x].x, t4.x, t4.y, t4.z, t4.w);
-                    res[8 * x + 5] = prologue_f16x4(hi[x].y, t5.x, t5.y, t5.z, t5.w);
-                    res[8 * x + 6] = prologue_f16x4(hi[x].z, t6.x, t6.y, t6.z, t6.w);
-                    res[8 * x + 7] = prologue_f16x4(hi[x].w, t7.x, t7.y, t7.z, t7.w);
-                } else {
-                    const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32;
-                    res[8 * x + 0] = prologue_f32x4(lo[x].x, tb);
-                    res[8 * x + 1] = prologue_f32x4(lo[x].y, tb + 4);
-                    res[8 * x + 2] = prologue_f32x4(lo[x].z, tb + 8);
-                    res[8 * x + 3] = prologue_f32x4(lo[x].w, tb + 12);
-                    res[8 * x + 4] = prologue_f32x4(hi[x].x, tb + 16);
-                    res[8 * x + 5] = prologue_f32x4(hi[x].y, tb + 20);
-                    res[8 * x + 6] = prologue_f32x4(hi[x].z, tb + 24);
-                    res[8 * x + 7] = prologue_f32x4(hi[x].w, tb + 28);
-                }
-            }
-            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
-            tc_fence_after();
-            tmem_st32(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8), res);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -454,9 +452,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         const int quad = warp & 3, half = (warp - 11) >> 2;
         const int ncol = NC >> 1;                              // columns of this warp
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
-        uint32_t arm[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
         for (int t = 0; t < my_tiles; ++t) {
             const int acc = t & 1;
             if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
@@ -465,11 +460,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int chunk = tile % a.nchunks;
             const int m = (tile / a.nchunks) * 128 + quad * 32 + lane;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
-            for (int cb = 0; cb < ncol; cb += 32) {
-                uint32_t v[32];
-                tmem_ld32(taddr + cb, v);
-                tmem_wait_ld();
-                tmem_st32(taddr + cb, arm);
+            // requantise 32 columns (output channels c0 ..) of this warp's 32 rows and store them
+            auto finish = [&](const uint32_t (&v)[32], int cb) {
                 const int c0 = chunk * NC + half * ncol + cb;      // first output channel
                 uint32_t wd[8];
 #pragma unroll
@@ -519,6 +511,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                             make_uint4(wd[4], wd[5], wd[6], wd[7]);
                     }
                 }
+            };
+            for (int cb = 0; cb < ncol; cb += 32) {
+                uint32_t v[32];
+                tmem_ld32(taddr + cb, v);
+                tmem_wait_ld();
+                tmem_fill32(taddr + cb, ACC_MAGIC);                 // re-arm for the tile after next
+                finish(v, cb);
             }
             tmem_wait_st();
             tc_fence_before();
