@@ -3,6 +3,7 @@
 // commit, TMEM loads, fences), UMMA descriptors and the bit-exact prologue arithmetic.
 #pragma once
 #include <cstdint>
+#include <cstring>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -52,12 +53,22 @@ DN8_DEV bool mbar_try(uint64_t* bar, uint32_t parity) {
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+// As mbar_try, but a thread whose phase is not complete is suspended until it completes or about
+// `ns` nanoseconds pass, so a waiting warp issues almost no instructions while it waits.
+DN8_DEV bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(ns) : "memory");
+    return ok != 0;
+}
 // Waits for the phase of parity `parity` to complete. Returns false (error raised) on timeout or
 // when another role has already aborted.
 DN8_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try(bar, parity)) {
+    while (!mbar_try_sleep(bar, parity, 100000u)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > WAIT_LIMIT) {
             raise_error(err, abort_flag, code);
@@ -184,34 +195,16 @@ constexpr uint32_t ACC_MAGIC = 0x4B400000u;
 constexpr float ACC_MAGIC_F = 12582912.0f;
 
 // ---- packed fp32 pairs (sm_100 f32x2) --------------------------------------------------------
-DN8_DEV unsigned long long f2_pack(float a, float b) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
+// Packed fp32 pairs (one f32x2 instruction for two lanes' worth of fp32 math, each element rounded
+// exactly as the scalar operation).
+DN8_DEV float2 f2_pack(float a, float b) { return make_float2(a, b); }
+DN8_DEV void f2_unpack(float2 r, float& a, float& b) {
+    a = r.x;
+    b = r.y;
 }
-DN8_DEV void f2_unpack(unsigned long long r, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-DN8_DEV unsigned long long f2_add(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-DN8_DEV unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
-    unsigned long long r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-DN8_DEV unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c) {
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-
-// ---- named barriers among a subset of warps -------------------------------------------------
-DN8_DEV void named_sync(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
+DN8_DEV float2 f2_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+DN8_DEV float2 f2_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+DN8_DEV float2 f2_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // ---- bit-exact prologue / epilogue arithmetic -----------------------------------------------
 // fp16 prologue of 4 store bytes (channels c..c+3, c even): u = rint(255 * sat_f16(A q + B)), the
@@ -219,17 +212,28 @@ DN8_DEV void named_sync(int id, int nthreads) {
 // in an fp16 (1024 + (q + 128) - 1152), one fp16 fma with saturation gives v, and a second fp16
 // fma v * 255 + 1024 rounds 255 v to the nearest integer (ties to even) in the low byte.
 // a01 / b01: (A, B) of channels c, c+1 as half2; a23 / b23 of c+2, c+3.
+DN8_DEV __half2 h2_of(uint32_t x) {
+    __half2 h;
+    memcpy(&h, &x, 4);
+    return h;
+}
+DN8_DEV uint32_t u32_of(__half2 h) {
+    uint32_t x;
+    memcpy(&x, &h, 4);
+    return x;
+}
 DN8_DEV uint32_t prologue_f16x4(uint32_t q4, uint32_t a01, uint32_t b01, uint32_t a23, uint32_t b23) {
     const uint32_t w = q4 ^ 0x80808080u;                 // signed byte q -> unsigned q + 128
-    uint32_t lo = __byte_perm(w, 0x64646464u, 0x4140);   // fp16 pair 1024 + (q + 128)
-    uint32_t hi = __byte_perm(w, 0x64646464u, 0x4342);
-    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(lo) : "r"(0xE480E480u));   // - 1152: exact q
-    asm("add.rn.f16x2 %0, %0, %1;" : "+r"(hi) : "r"(0xE480E480u));
-    asm("fma.rn.sat.f16x2 %0, %0, %1, %2;" : "+r"(lo) : "r"(a01), "r"(b01));
-    asm("fma.rn.sat.f16x2 %0, %0, %1, %2;" : "+r"(hi) : "r"(a23), "r"(b23));
-    asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(lo) : "r"(0x5BF85BF8u), "r"(0x64006400u));  // *255 +1024
-    asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(hi) : "r"(0x5BF85BF8u), "r"(0x64006400u));
-    return __byte_perm(lo, hi, 0x6420);
+    __half2 lo = h2_of(__byte_perm(w, 0x64646464u, 0x4140));   // fp16 pair 1024 + (q + 128)
+    __half2 hi = h2_of(__byte_perm(w, 0x64646464u, 0x4342));
+    const __half2 m1152 = h2_of(0xE480E480u), k255 = h2_of(0x5BF85BF8u), k1024 = h2_of(0x64006400u);
+    lo = __hadd2(lo, m1152);                             // - 1152: exact q
+    hi = __hadd2(hi, m1152);
+    lo = __hfma2_sat(lo, h2_of(a01), h2_of(b01));
+    hi = __hfma2_sat(hi, h2_of(a23), h2_of(b23));
+    lo = __hfma2(lo, k255, k1024);                       // * 255 + 1024
+    hi = __hfma2(hi, k255, k1024);
+    return __byte_perm(u32_of(lo), u32_of(hi), 0x6420);
 }
 
 // fp32 prologue of one store byte `q` (the reference's `pro16`, :99-120): v = sat(fmaf(a, q, b)),

@@ -301,16 +301,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         // ---------------- prologue, A into TMEM (conv1) ----------------
         // Warp w writes TMEM lanes 32 (w % 4) .. + 31, so the four warps of one lane quadrant each
         // take a quarter of the stage's rows: row r = 32 q + lane, all 4 units (K groups) of the
-        // stage; the two warps of a quadrant alternate stages. The 32 raw bytes of a row are read
-        // half-swapped on odd row quads so that a warp's 16-byte reads hit all 32 banks.
+        // stage; the two warps of a quadrant alternate stages.
         const int q = warp & 3, kk = (warp - 3) >> 2;
         const int r = q * 32 + lane;
-        const int sw = (r >> 2) & 1;
         const uint32_t tlane = static_cast<uint32_t>(q * 32) << 16;
+        int j = kk;                                   // stage index within the tile (i = t * NS + j)
+        while (j >= NS) j -= NS;
         for (int i = kk; i < T; i += 2) {
             const int s = i % SR, sa = i % SA;
-            const int t = i / NS, j = i - t * NS;
             const int gc = min(KSTEP, G - j * KSTEP);
+            const int j_this = j;
+            j += 2;
+            while (j >= NS) j -= NS;
             if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
             if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
             tc_fence_after();
@@ -318,11 +320,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 #pragma unroll
             for (int x = 0; x < UNITS; ++x) {
                 if (x >= gc) break;
-                const int g = j * KSTEP + x;
+                const int g = j_this * KSTEP + x;
+                // (2-way bank conflicts on these two reads cost less than swapping the halves)
                 const uint8_t* src = sR + s * RB + x * 4096 + r * 32;
-                const uint4 v0 = *reinterpret_cast<const uint4*>(src + sw * 16);
-                const uint4 v1 = *reinterpret_cast<const uint4*>(src + (sw ^ 1) * 16);
-                const uint4 lo = sw ? v1 : v0, hi = sw ? v0 : v1;
+                const uint4 lo = *reinterpret_cast<const uint4*>(src);
+                const uint4 hi = *reinterpret_cast<const uint4*>(src + 16);
                 uint32_t res[8];
                 if (F16) {
                     const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128);   // 32 channels
@@ -457,12 +459,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
             tc_fence_after();
             const int tile = blockIdx.x + t * gridDim.x;
-            const int chunk = tile % a.nchunks;
-            const int m = (tile / a.nchunks) * 128 + quad * 32 + lane;
+            const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
+            const int chunk = tile % nch;
+            const int m = (tile / nch) * 128 + quad * 32 + lane;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
             // requantise 32 columns (output channels c0 ..) of this warp's 32 rows and store them
             auto finish = [&](const uint32_t (&v)[32], int cb) {
-                const int c0 = chunk * NC + half * ncol + cb;      // first output channel
+                const int c0 = chunk * NC + half * ncol + cb;      // first output channel (even)
+                const float4* gdp = gd4 + (c0 >> 1);               // (g, d) pairs of channels c0 ..
                 uint32_t wd[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -470,26 +474,24 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int c = 4 * j + 2 * e;
+                        // scalar ops with immediate constants: packed pairs of constants would cost
+                        // register moves
                         float f0, f1;
                         if (fast_cvt) {
-                            f2_unpack(f2_add(f2_pack(__uint_as_float(v[c]), __uint_as_float(v[c + 1])),
-                                             f2_pack(-ACC_MAGIC_F, -ACC_MAGIC_F)), f0, f1);
+                            f0 = __uint_as_float(v[c]) - ACC_MAGIC_F;
+                            f1 = __uint_as_float(v[c + 1]) - ACC_MAGIC_F;
                         } else {
                             f0 = __int2float_rn(static_cast<int32_t>(v[c] - ACC_MAGIC));
                             f1 = __int2float_rn(static_cast<int32_t>(v[c + 1] - ACC_MAGIC));
                         }
-                        const float4 p = gd4[(c0 + c) >> 1];           // (g, d) of channels c0+c, c0+c+1
+                        const float4 p = gdp[c >> 1];                  // (g, d) of channels c0+c, c0+c+1
                         float r0, r1;
                         if (TRANS) {
-                            f2_unpack(f2_mul(f2_pack(p.x, p.z), f2_pack(f0, f1)), r0, r1);
-                            r0 = fminf(fmaxf(r0, -127.0f), 127.0f);
-                            r1 = fminf(fmaxf(r1, -127.0f), 127.0f);
-                            f2_unpack(f2_add(f2_pack(r0, r1), f2_pack(12582912.0f, 12582912.0f)), r0, r1);
+                            r0 = fminf(fmaxf(p.x * f0, -127.0f), 127.0f) + 12582912.0f;
+                            r1 = fminf(fmaxf(p.z * f1, -127.0f), 127.0f) + 12582912.0f;
                         } else {
-                            const float u0 = __saturatef(fmaf(p.x, f0, p.y));
-                            const float u1 = __saturatef(fmaf(p.z, f1, p.w));
-                            f2_unpack(f2_fma(f2_pack(u0, u1), f2_pack(255.0f, 255.0f),
-                                             f2_pack(8388608.0f, 8388608.0f)), r0, r1);
+                            r0 = fmaf(__saturatef(fmaf(p.x, f0, p.y)), 255.0f, 8388608.0f);
+                            r1 = fmaf(__saturatef(fmaf(p.z, f1, p.w)), 255.0f, 8388608.0f);
                         }
                         b[2 * e] = __float_as_uint(r0);
                         b[2 * e + 1] = __float_as_uint(r1);

@@ -325,20 +325,15 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                     uint32_t wd[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        // k, c of the 4 channels (broadcast reads); fmaf pairwise in f32x2
+                        // k, c of the 4 channels (broadcast reads); fmaf pairwise in f32x2 (the k, c pairs
+                        // come straight from the float4 reads)
                         const float4 k4 = *reinterpret_cast<const float4*>(sKC + hc * 32 + 4 * j);
                         const float4 c4 = *reinterpret_cast<const float4*>(sKC + 64 + hc * 32 + 4 * j);
                         float f[4];
 #pragma unroll
-                        for (int e = 0; e < 4; e += 2) {
-                            if (fast_cvt) {
-                                f2_unpack(f2_add(f2_pack(__uint_as_float(v[4 * j + e]), __uint_as_float(v[4 * j + e + 1])),
-                                                 f2_pack(-ACC_MAGIC_F, -ACC_MAGIC_F)), f[e], f[e + 1]);
-                            } else {
-                                f[e] = __int2float_rn(static_cast<int32_t>(v[4 * j + e] - ACC_MAGIC));
-                                f[e + 1] = __int2float_rn(static_cast<int32_t>(v[4 * j + e + 1] - ACC_MAGIC));
-                            }
-                        }
+                        for (int e = 0; e < 4; ++e)
+                            f[e] = fast_cvt ? __uint_as_float(v[4 * j + e]) - ACC_MAGIC_F
+                                            : __int2float_rn(static_cast<int32_t>(v[4 * j + e] - ACC_MAGIC));
                         float tq[4];
                         f2_unpack(f2_fma(f2_pack(f[0], f[1]), f2_pack(k4.x, k4.y), f2_pack(c4.x, c4.y)), tq[0], tq[1]);
                         f2_unpack(f2_fma(f2_pack(f[2], f[3]), f2_pack(k4.z, k4.w), f2_pack(c4.z, c4.w)), tq[2], tq[3]);
