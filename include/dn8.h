@@ -135,6 +135,17 @@ typedef struct dn8_head_args {
 } dn8_head_args;
 int dn8_head(const dn8_head_args* a, dn8_stream stream);
 
+/* dn8_head without a caller-provided ticket array (no counterpart in the reference): the per-view
+ * counters live in a scratch array built into the library, DN8_HEAD_SCRATCH_VIEWS int32 per device,
+ * so the call allocates nothing. a->tickets must be NULL; N / per_view above DN8_HEAD_SCRATCH_VIEWS
+ * is rejected with DN8_EINVAL before any CUDA call. The scratch starts at zero and every completed
+ * call leaves it zero. The first call on a device looks the scratch up (cudaGetSymbolAddress, which
+ * can load the module on that device): make it before any stream capture. Calls that may overlap
+ * (on several streams, or several threads, of one device) share the scratch and race: issue them
+ * in order on one stream. */
+#define DN8_HEAD_SCRATCH_VIEWS 4096
+int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream);
+
 /* ---- weight preparation (host memory to host memory, once per pack) ------------------------
  * The kernels read their weights with bulk copies straight into the tensor cores' shared-memory
  * operand layout; these functions permute the reference pack tables into that layout. */

@@ -8,6 +8,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libdn8b200.so")
 DN8_OK, DN8_EINVAL, DN8_ECUDA, DN8_EDEVICE = 0, 1, 2, 3
+DN8_HEAD_SCRATCH_VIEWS = 4096
 P, I32 = ctypes.c_void_p, ctypes.c_int32
 
 
@@ -65,6 +66,7 @@ EXPORTS = {
     "dn8_trans": ([ctypes.POINTER(TransArgs), P], ctypes.c_int),
     "dn8_stem": ([ctypes.POINTER(StemArgs), P], ctypes.c_int),
     "dn8_head": ([ctypes.POINTER(HeadArgs), P], ctypes.c_int),
+    "dn8_head_noalloc": ([ctypes.POINTER(HeadArgs), P], ctypes.c_int),
     "dn8_prepare_stem_weights": ([P, P], ctypes.c_int),
     "dn8_prepare_conv1_weights": ([P, I32, P], ctypes.c_int),
     "dn8_prepare_trans_weights": ([P, I32, I32, P], ctypes.c_int),

@@ -161,6 +161,31 @@ int dn8_head(const dn8_head_args* a, dn8_stream stream) {
     return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_head launch");
 }
 
+int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
+    if (a == nullptr) return fail(DN8_EINVAL, "dn8_head_noalloc: null arguments");
+    if (a->view_logits != nullptr && a->per_view >= 1 && a->N % a->per_view == 0 &&
+        a->N / a->per_view > DN8_HEAD_SCRATCH_VIEWS)
+        return fail(DN8_EINVAL, "dn8_head_noalloc: %d views (N / per_view), the built-in scratch holds %d",
+                    a->N / a->per_view, DN8_HEAD_SCRATCH_VIEWS);
+    if (a->tickets != nullptr)
+        return fail(DN8_EINVAL, "dn8_head_noalloc: tickets must be NULL (the built-in scratch is used)");
+    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64)
+        return fail(DN8_EINVAL, "dn8_head_noalloc: bad geometry");
+    if (!aligned16(a->in0) || !aligned16(a->seg) || a->fab == nullptr)
+        return fail(DN8_EINVAL, "dn8_head_noalloc: bad pointers");
+    if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
+        return fail(DN8_EINVAL, "dn8_head_noalloc: head without bias or logits buffer");
+    if (a->view_logits != nullptr && (a->per_view < 1 || a->N % a->per_view))
+        return fail(DN8_EINVAL, "dn8_head_noalloc: views need per_view dividing N");
+    dn8_head_args args = *a;
+    if (args.view_logits != nullptr) {
+        cudaError_t e = dn8::head_scratch_tickets(&args.tickets);
+        if (e != cudaSuccess) return cuda_fail(e, "dn8_head_noalloc scratch address");
+    }
+    cudaError_t e = dn8::launch_head(args, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_head_noalloc launch");
+}
+
 int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out) {
     if (w8 == nullptr || out == nullptr) return fail(DN8_EINVAL, "dn8_prepare_stem_weights: bad arguments");
     // S_w8 [64][176] -> 6 K steps of [64 rows][32 B], K bytes 176 .. 191 zero, 32B-swizzled

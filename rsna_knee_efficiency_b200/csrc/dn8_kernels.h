@@ -14,6 +14,8 @@ cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st);
 int trans_chunk(int cout);
 cudaError_t launch_stem(const dn8_stem_args& a, int sms, cudaStream_t st);
 cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st);
+constexpr int DN8_MAX_DEVICES = 64;
+cudaError_t head_scratch_tickets(int32_t** out);
 
 struct Conv2Plan {
     CUtensorMap map;      // bottleneck planes, built once per geometry and buffer

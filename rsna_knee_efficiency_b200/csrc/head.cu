@@ -6,6 +6,8 @@
 //   logits l[n][j] = sum_c f[n][c] * Hw[j][c] + Hb[j] (fp32, fixed reduction order);
 //   per view of V consecutive images the mean of the logits over the view (the slice mean), written
 //   by the last CTA of the view to finish (an atomic ticket per view, reset for the next call).
+#include <mutex>
+
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
@@ -93,6 +95,33 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
         }
         if (tid == 0) a.tickets[v] = 0;
     }
+}
+
+// Built-in ticket scratch of dn8_head_noalloc: one counter per view, zero at module load and left
+// zero by every completed call (the last image of a view resets its counter).
+static __device__ __align__(256) int32_t g_view_tickets[DN8_HEAD_SCRATCH_VIEWS];
+
+namespace {
+std::mutex g_scratch_mu;
+int32_t* g_scratch_ptr[DN8_MAX_DEVICES] = {};
+}  // namespace
+
+// Device address of the current device's ticket scratch, looked up once per device (the first
+// call can load the module on that device, so it should not happen inside stream capture).
+cudaError_t head_scratch_tickets(int32_t** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= DN8_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_view_tickets);
+        if (e != cudaSuccess) return e;
+        g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+    }
+    *out = g_scratch_ptr[dev];
+    return cudaSuccess;
 }
 
 cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st) {

@@ -63,6 +63,18 @@ def head(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: in
     nat.check(nat.lib().dn8_head(a, _stream(stream)), "dn8_head")
 
 
+def head_noalloc(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: int, N: int, HW: int,
+                 feat: torch.Tensor | None = None, hw: torch.Tensor | None = None, hb: torch.Tensor | None = None,
+                 logits: torch.Tensor | None = None, view_logits: torch.Tensor | None = None,
+                 per_view: int = 0, stream=None) -> None:
+    """`head` with the library's built-in per-view counters instead of a ticket array (no device
+    allocation by the caller): at most DN8_HEAD_SCRATCH_VIEWS views per call, calls in order."""
+    n_out = 0 if hw is None else hw.shape[0]
+    a = nat.HeadArgs(_ptr(in0), _ptr(seg), _ptr(fab), _ptr(feat), _ptr(hw), _ptr(hb), _ptr(logits),
+                     _ptr(view_logits), None, G0, G, N, HW, n_out, per_view, 0)
+    nat.check(nat.lib().dn8_head_noalloc(a, _stream(stream)), "dn8_head_noalloc")
+
+
 # --- weight preparation (numpy in, numpy out) ----------------------------------------------
 def prepare_stem_weights(w8: np.ndarray) -> np.ndarray:
     """`S_w8` [64, 176] int8 -> the stem operand table (12288 bytes)."""
