@@ -93,6 +93,8 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
+    griddep_launch_dependents();
+    griddep_wait();                                    // the bottleneck of this layer's conv1
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -285,7 +287,7 @@ cudaError_t prepare_conv2(Conv2Plan* plan, const dn8_conv2_args& a) {
     return make_bott_map(&plan->map, a.x, a.N, a.H, a.W, plan->Rt);
 }
 
-cudaError_t launch_conv2(const Conv2Plan& plan, const dn8_conv2_args& a, int sms, cudaStream_t st) {
+cudaError_t launch_conv2(const Conv2Plan& plan, const dn8_conv2_args& a, int sms, cudaStream_t st, bool pdl) {
     const int tpi = (a.H + plan.Rt - 1) / plan.Rt;
     const int ntiles = a.N * tpi;
     const int grid = ntiles < sms ? ntiles : sms;
@@ -293,8 +295,8 @@ cudaError_t launch_conv2(const Conv2Plan& plan, const dn8_conv2_args& a, int sms
     cudaError_t e = cudaFuncSetAttribute(conv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(plan.smem));
     if (e != cudaSuccess) return e;
-    conv2_kernel<<<grid, C2_THREADS, plan.smem, st>>>(plan.map, a, plan.Rt, plan.stage_bytes);
-    return cudaGetLastError();
+    return launch_pdl(pdl, conv2_kernel, dim3(grid), dim3(C2_THREADS), plan.smem, st, plan.map, a, plan.Rt,
+                      plan.stage_bytes);
 }
 
 }  // namespace dn8

@@ -78,6 +78,14 @@ DN8_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* a
     return true;
 }
 
+// ---- programmatic dependent launch -----------------------------------------------------------
+// Kernels are launched with programmatic stream serialization: the next kernel of the stream may
+// start (and do its setup: barriers, TMEM, constant tables) while this one finishes. Every kernel
+// lets its dependents launch once its own setup is done, then waits for its predecessor's
+// completion (and memory) before it reads activations or writes any output.
+DN8_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+DN8_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- bulk copies / TMA ----------------------------------------------------------------------
 // Contiguous global -> shared copy (16-byte aligned, size a multiple of 16), completing on `bar`.
 DN8_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -299,14 +299,14 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
             c1.in0 = in0; c1.seg = seg; c1.w = reinterpret_cast<const int8_t*>(ly.w1); c1.ab = ly.ab; c1.gd = ly.gd;
             c1.out = e->bott; c1.err = e->err; c1.G0 = G0; c1.G = G0 + l; c1.N = cap; c1.HW = HW;
             c1.prologue_f16 = e->c1_f16[b][l];
-            if ((ce = dn8::launch_conv1(c1, e->sms, st)) != cudaSuccess)
+            if ((ce = dn8::launch_conv1(c1, e->sms, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv1 b%d l%d: %s", b, l, cudaGetErrorString(ce));
             mark(e, DN8_K_CONV1, b, l, st);
             dn8_conv2_args c2{};
             c2.x = e->bott; c2.w = reinterpret_cast<const int8_t*>(ly.w2); c2.sc = ly.c2;
             c2.out = seg + static_cast<size_t>(l) * cap * HW * 32; c2.err = e->err;
             c2.N = cap; c2.H = e->h[b]; c2.W = e->w[b];
-            if ((ce = dn8::launch_conv2(e->c2plan[b], c2, e->sms, st)) != cudaSuccess)
+            if ((ce = dn8::launch_conv2(e->c2plan[b], c2, e->sms, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv2 b%d l%d: %s", b, l, cudaGetErrorString(ce));
             mark(e, DN8_K_CONV2, b, l, st);
         }
@@ -315,7 +315,7 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
             t.in0 = in0; t.seg = seg; t.w = reinterpret_cast<const int8_t*>(e->tw[b]); t.ab = e->tab[b]; t.gd = e->tgd[b];
             t.out = e->arena[(b + 1) % 2]; t.err = e->err;
             t.G0 = G0; t.G = G0 + e->L[b]; t.N = cap; t.H = e->h[b]; t.W = e->w[b]; t.prologue_f16 = e->trans_f16[b];
-            if ((ce = dn8::launch_trans(t, e->sms, st)) != cudaSuccess)
+            if ((ce = dn8::launch_trans(t, e->sms, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "transition %d: %s", b, cudaGetErrorString(ce));
             mark(e, DN8_K_TRANS, b, 0, st);
         } else {
@@ -330,7 +330,7 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
             hd.tickets = e->tickets;
             hd.G0 = G0; hd.G = G0 + e->L[b]; hd.N = n; hd.HW = HW; hd.n_out = e->n_out; hd.per_view = per_view;
             hd.n_alloc = cap;
-            if ((ce = dn8::launch_head(hd, st)) != cudaSuccess) return efail(e, DN8_ECUDA, "head: %s", cudaGetErrorString(ce));
+            if ((ce = dn8::launch_head(hd, st, true)) != cudaSuccess) return efail(e, DN8_ECUDA, "head: %s", cudaGetErrorString(ce));
             mark(e, DN8_K_HEAD, b, 0, st);
         }
     }

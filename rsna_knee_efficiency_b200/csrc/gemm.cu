@@ -186,6 +186,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     tc_fence_before();
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
+    griddep_launch_dependents();
+    griddep_wait();                                    // the previous layer's store / bottleneck
 
     if (warp == 0) {
         // ---------------- MMA issuer ----------------
@@ -537,7 +539,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 }
 
 template <bool F16, bool TRANS>
-static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st) {
+static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
     const size_t smem = gemm_layout(TRANS, g.G, g.nc, g.nchunks, g.raw_bytes, &g.sb, &g.b_resident) + 1024;
     if (smem > 227 * 1024 || g.sb < 2) return cudaErrorInvalidConfiguration;
     const int ntiles = ((g.rows + 127) / 128) * g.nchunks;
@@ -546,18 +548,17 @@ static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, TRANS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    gemm_kernel<F16, TRANS><<<grid, GM_THREADS, smem, st>>>(g);
-    return cudaGetLastError();
+    return launch_pdl(pdl, gemm_kernel<F16, TRANS>, dim3(grid), dim3(GM_THREADS), smem, st, g);
 }
 
-cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st) {
+cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool pdl) {
     GemmArgs g{};
     g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
     g.out = a.out; g.err = a.err;
     g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.HW; g.W = 0;
     g.rows = a.N * a.HW; g.cout = 128; g.nc = 128; g.nchunks = 1;
     g.raw_bytes = 4 * 4096;
-    return a.prologue_f16 ? launch_gemm<true, false>(g, sms, st) : launch_gemm<false, false>(g, sms, st);
+    return a.prologue_f16 ? launch_gemm<true, false>(g, sms, st, pdl) : launch_gemm<false, false>(g, sms, st, pdl);
 }
 
 // output channels per CTA tile: 256 when it divides c_out (TMEM: 2 x 256 columns), else 128
@@ -572,7 +573,7 @@ static int trans_raw_bytes(int W) {
     return ((2 * prow * W * 32 + 1023) / 1024) * 1024;
 }
 
-cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st) {
+cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st, bool pdl) {
     GemmArgs g{};
     const int cout = a.G * 16;
     g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
@@ -580,7 +581,7 @@ cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st) {
     g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.H * a.W; g.W = a.W;
     g.rows = a.N * (a.H / 2) * (a.W / 2); g.cout = cout; g.nc = trans_chunk(cout); g.nchunks = cout / g.nc;
     g.raw_bytes = trans_raw_bytes(a.W);
-    return a.prologue_f16 ? launch_gemm<true, true>(g, sms, st) : launch_gemm<false, true>(g, sms, st);
+    return a.prologue_f16 ? launch_gemm<true, true>(g, sms, st, pdl) : launch_gemm<false, true>(g, sms, st, pdl);
 }
 
 }  // namespace dn8

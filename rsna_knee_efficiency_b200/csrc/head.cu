@@ -23,6 +23,8 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
     float* feat = hs + 4 * C;                  // [C]
     float* red = feat + C;                     // [HD_THREADS / 32][NOUT]
     const int tid = threadIdx.x;
+    griddep_launch_dependents();
+    griddep_wait();                            // the last block's store
     // task = (group g, half h, partial q): 16 channels, pixels q, q + 4, ...
     for (int task = tid; task < a.G * 8; task += HD_THREADS) {
         const int g = task >> 3, h = (task >> 2) & 1, q = task & 3;
@@ -124,14 +126,13 @@ cudaError_t head_scratch_tickets(int32_t** out) {
     return cudaSuccess;
 }
 
-cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st) {
+cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st, bool pdl) {
     const int C = a.G * 32;
     const size_t smem = (static_cast<size_t>(5) * C + (HD_THREADS / 32) * (a.n_out > 0 ? a.n_out : 1)) * sizeof(float);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    head_kernel<<<a.N, HD_THREADS, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(pdl, head_kernel, dim3(a.N), dim3(HD_THREADS), smem, st, a);
 }
 
 }  // namespace dn8

@@ -125,6 +125,8 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     tc_fence_before();
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
+    griddep_launch_dependents();
+    griddep_wait();                                    // pixels, and the readers of block 1's input
 
     // conv rows of task t: band b of image n -> conv rows cr0 .. cr0 + nrows - 1
     auto task_rows = [&](int t, int& n, int& py0, int& cr0, int& nrows) {
@@ -422,8 +424,8 @@ cudaError_t launch_stem(const dn8_stem_args& a, int sms, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(stem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(geo.smem));
     if (e != cudaSuccess) return e;
-    stem_kernel<<<grid, ST_THREADS, geo.smem, st>>>(a, geo);
-    return cudaGetLastError();
+    // the first kernel of a pass: its predecessor may be anything (a copy, an event wait)
+    return launch_pdl(false, stem_kernel, dim3(grid), dim3(ST_THREADS), geo.smem, st, a, geo);
 }
 
 }  // namespace dn8
