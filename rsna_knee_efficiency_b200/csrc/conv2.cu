@@ -93,15 +93,18 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
+    if (threadIdx.x == 0 && my_tiles > 0) {
+        // the prepared weights [dy][cblk][half][dx * 32 + o][16] in one bulk copy (constant: it
+        // may land while the previous kernel still runs)
+        mbar_expect_tx(&wfull[0], C2_W_BYTES);
+        bulk_g2s(sW, a.w, C2_W_BYTES, &wfull[0]);
+    }
     griddep_launch_dependents();
     griddep_wait();                                    // the bottleneck of this layer's conv1
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0 && my_tiles > 0) {
-            // the prepared weights [dy][cblk][half][dx * 32 + o][16] in one bulk copy
-            mbar_expect_tx(&wfull[0], C2_W_BYTES);
-            bulk_g2s(sW, a.w, C2_W_BYTES, &wfull[0]);
             for (int t = 0; t < my_tiles; ++t) {
                 const int s = t % C2_STAGES;
                 if (!mbar_wait(&empty[s], ((t / C2_STAGES) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;

@@ -186,6 +186,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     tc_fence_before();
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
+    if (warp == 2 && lane == 0 && T > 0 && a.b_resident) {
+        // resident weights (constant: they may land while the previous kernel still runs)
+        mbar_expect_tx(&fullB[0], static_cast<uint32_t>(G * btile));
+        bulk_g2s(sB, a.wu, static_cast<uint32_t>(G * btile), &fullB[0]);
+    }
     griddep_launch_dependents();
     griddep_wait();                                    // the previous layer's store / bottleneck
 
@@ -276,10 +281,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     } else if (warp == 2) {
         // ---------------- weight producer ----------------
         if (lane == 0 && T > 0) {
-            if (a.b_resident) {
-                mbar_expect_tx(&fullB[0], static_cast<uint32_t>(G * btile));
-                bulk_g2s(sB, a.wu, static_cast<uint32_t>(G * btile), &fullB[0]);
-            } else {
+            if (!a.b_resident) {
                 int i = 0;
                 for (int t = 0; t < my_tiles; ++t) {
                     const int tile = blockIdx.x + t * gridDim.x;

@@ -79,16 +79,17 @@ class StudyRunner:
         return self.out
 
 
-def run_shard(runner, volumes, rank: int = 0, world: int = 1) -> torch.Tensor:
-    """Study logits [n_local, n_out] (float32, host) of this rank's contiguous shard of `volumes`
-    (uint8 [windows, n_studies, S, H, W] in host memory, pinned for overlap): batches of
-    `runner.studies` studies are copied to the device on a copy stream (two staging buffers, the
-    next batch's copy overlapping this batch's encoders), run, and their logits read back into
-    pinned host memory; the last batch is padded by repeating its last study. `runner` needs
-    `studies`, `device`, `n_out` and `run(volumes_on_device)` (on the current stream)."""
-    n = volumes.shape[1]
-    start, end = shard(n, world, rank)
+def run_shard(runner, volumes, rank: int = 0, world: int = 1, studies=None) -> torch.Tensor:
+    """Study logits [n_local, n_out] (float32, host) of this rank's contiguous shard of the studies
+    (`studies`: indices into `volumes`, default all of them, in order; `volumes`: uint8 [windows,
+    n_volumes, S, H, W] in host memory, pinned for overlap). Batches of `runner.studies` studies are
+    copied to the device on a copy stream (two staging buffers, the next batch's copy overlapping
+    this batch's encoders), run, and their logits read back into pinned host memory; the last batch
+    is padded by repeating its last study. `runner` needs `studies`, `device`, `n_out` and
+    `run(volumes_on_device)` (on the current stream)."""
     vols = torch.as_tensor(volumes)
+    order = list(range(vols.shape[1])) if studies is None else [int(k) for k in studies]
+    start, end = shard(len(order), world, rank)
     B, dev = runner.studies, runner.device
     starts = list(range(start, end, B))
     on_gpu = str(dev).startswith("cuda")
@@ -98,8 +99,16 @@ def run_shard(runner, volumes, rank: int = 0, world: int = 1) -> torch.Tensor:
 
     def fill(st, s0):
         k = min(B, end - s0)
-        for w in range(st.shape[0]):                 # one contiguous copy per window
-            st[w, :k].copy_(vols[w, s0:s0 + k], non_blocking=True)
+        idx = order[s0:s0 + k]
+        runs = []                                    # contiguous runs of volume indices
+        for b, v in enumerate(idx):
+            if runs and v == runs[-1][1] + runs[-1][2]:
+                runs[-1][2] += 1
+            else:
+                runs.append([b, v, 1])
+        for w in range(st.shape[0]):                 # one copy per window and run
+            for b, v, c in runs:
+                st[w, b:b + c].copy_(vols[w, v:v + c], non_blocking=True)
         if k < B:
             st[:, k:].copy_(st[:, k - 1:k].expand(-1, B - k, *st.shape[2:]))
         return k

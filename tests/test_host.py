@@ -188,3 +188,13 @@ def test_bench_work_model_matches_the_per_image_totals():
         tb, tm = tb + by, tm + m
     assert abs(tb / 1e6 - 128.12) < 0.01
     assert abs(tm / 1e9 - 17.545) < 0.001
+
+
+def test_run_shard_with_study_indices():
+    """`studies` picks (and may repeat) volumes; shards follow that order."""
+    vols = infer.make_volumes(4, img=16, slices=4, seed=21)
+    order = [2, 0, 1, 1, 3, 2, 0]
+    want = _expected(vols)[order]
+    torch.testing.assert_close(infer.run_shard(_FakeRunner(3), vols, studies=order), want)
+    a, b = infer.shard(len(order), 2, 1)
+    torch.testing.assert_close(infer.run_shard(_FakeRunner(2), vols, rank=1, world=2, studies=order), want[a:b])
