@@ -146,6 +146,24 @@ int dn8_head(const dn8_head_args* a, dn8_stream stream);
 #define DN8_HEAD_SCRATCH_VIEWS 4096
 int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream);
 
+/* geometric test-time view: replaces `affine_windows` (src/knee/tta.py:131-149; zoom `scale` about
+ * the centre, shift (tx, ty) as fractions of the side, bilinear, zero outside, align_corners =
+ * False, in fp16) applied to the windows the reference gathers from the uint8 volume
+ * (`gather_u8_to_f16`, src/knee/data/fused_uint8.py:480-505). Reads the uint8 planes [P][H][W]
+ * through src[N][4] (planes of channels 0-2), flags[N] bit 0 = mirror the window first; writes the
+ * fp16 windows [N][3][H][W] that dn8_stem (x_u8 = 0) or the engine read. W a multiple of 16,
+ * scale >= 0.25. */
+typedef struct dn8_zoom_args {
+    const uint8_t* planes;
+    const int32_t* src;
+    const int32_t* flags;   /* [N] or NULL */
+    uint16_t* out;          /* fp16 [N][3][H][W] */
+    int32_t* err;
+    int32_t N, H, W;
+    double scale, tx, ty;   /* as the reference's Python floats */
+} dn8_zoom_args;
+int dn8_zoom(const dn8_zoom_args* a, dn8_stream stream);
+
 /* ---- weight preparation (host memory to host memory, once per pack) ------------------------
  * The kernels read their weights with bulk copies straight into the tensor cores' shared-memory
  * operand layout; these functions permute the reference pack tables into that layout. */

@@ -39,6 +39,12 @@ class HeadArgs(ctypes.Structure):
                 ("n_alloc", I32)]
 
 
+class ZoomArgs(ctypes.Structure):
+    _fields_ = [("planes", P), ("src", P), ("flags", P), ("out", P), ("err", P),
+                ("N", I32), ("H", I32), ("W", I32), ("scale", ctypes.c_double), ("tx", ctypes.c_double),
+                ("ty", ctypes.c_double)]
+
+
 class Table(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char_p), ("data", P), ("nbytes", ctypes.c_int64)]
 
@@ -67,6 +73,7 @@ EXPORTS = {
     "dn8_stem": ([ctypes.POINTER(StemArgs), P], ctypes.c_int),
     "dn8_head": ([ctypes.POINTER(HeadArgs), P], ctypes.c_int),
     "dn8_head_noalloc": ([ctypes.POINTER(HeadArgs), P], ctypes.c_int),
+    "dn8_zoom": ([ctypes.POINTER(ZoomArgs), P], ctypes.c_int),
     "dn8_prepare_stem_weights": ([P, P], ctypes.c_int),
     "dn8_prepare_conv1_weights": ([P, I32, P], ctypes.c_int),
     "dn8_prepare_trans_weights": ([P, I32, I32, P], ctypes.c_int),

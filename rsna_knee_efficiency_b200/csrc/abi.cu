@@ -161,6 +161,18 @@ int dn8_head(const dn8_head_args* a, dn8_stream stream) {
     return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_head launch");
 }
 
+int dn8_zoom(const dn8_zoom_args* a, dn8_stream stream) {
+    if (a == nullptr) return fail(DN8_EINVAL, "dn8_zoom: null arguments");
+    if (a->N < 1 || a->H < 2 || a->W < 16 || a->W % 16 || !(a->scale >= 0.25) || a->planes == nullptr || a->src == nullptr ||
+        a->out == nullptr)
+        return fail(DN8_EINVAL, "dn8_zoom: bad arguments N=%d H=%d W=%d scale=%g", a->N, a->H, a->W,
+                    a->scale);
+    int sms = 0;
+    if (int s = current_sms(&sms)) return s;
+    cudaError_t e = dn8::launch_zoom(*a, sms, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_zoom launch");
+}
+
 int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
     if (a == nullptr) return fail(DN8_EINVAL, "dn8_head_noalloc: null arguments");
     if (a->view_logits != nullptr && a->per_view >= 1 && a->N % a->per_view == 0 &&

@@ -33,6 +33,7 @@ cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st, bool
 int trans_chunk(int cout);
 cudaError_t launch_stem(const dn8_stem_args& a, int sms, cudaStream_t st);
 cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st, bool pdl = false);
+cudaError_t launch_zoom(const dn8_zoom_args& a, int sms, cudaStream_t st);
 constexpr int DN8_MAX_DEVICES = 64;
 cudaError_t head_scratch_tickets(int32_t** out);
 

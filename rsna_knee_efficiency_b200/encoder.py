@@ -158,6 +158,24 @@ class Dense8SEncoder:
         cur.wait_stream(self.stream)
         return self.out[:n]
 
+    def encode(self, x: torch.Tensor, logits: torch.Tensor | None = None, views: torch.Tensor | None = None,
+               per_view: int = 0) -> torch.Tensor:
+        """`encode_u8` for fp16 windows x (N, 3, img, img) on cuda:dev (e.g. the zoomed view of
+        `ops.zoom`): features out[:N], and the head's logits / per-view means when given."""
+        n = x.shape[0]
+        if x.dtype != torch.float16 or tuple(x.shape[1:]) != self.in_shape[1:]:
+            raise ValueError(f"encode: fp16 (N, {', '.join(map(str, self.in_shape[1:]))}) expected")
+        x = x.contiguous()
+        cur = torch.cuda.current_stream(self.dev)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            self._forward(nat.Input(x.data_ptr(), None, None, 0), n, self.out.data_ptr(),
+                          None if logits is None else logits.data_ptr(),
+                          None if views is None else views.data_ptr(), per_view)
+            self._last_input = x
+        cur.wait_stream(self.stream)
+        return self.out[:n]
+
     def check(self) -> None:
         """Raises if a kernel gave up a bounded wait since the last check (synchronises)."""
         nat.check(nat.lib().dn8_engine_check(self._h, self.stream.cuda_stream), "dn8_engine_check", self._h)

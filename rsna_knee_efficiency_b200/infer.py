@@ -35,8 +35,12 @@ class StudyRunner:
     the planes of one window of all the call's studies are contiguous)."""
 
     def __init__(self, packs: list[dict], dev: int, studies: int, slices: int = 26,
-                 flip_tta: bool = False) -> None:
+                 flip_tta: bool = False, zoom: tuple | None = None) -> None:
+        """`zoom` = (scale, tx, ty): the geometric view of the reference's TTA (`affine_windows`,
+        src/knee/tta.py:131-149; the submission's view is (1.10, 0, 0)): the windows are zoomed on the
+        device (`ops.zoom`) and encoded through the fp16 path instead of the stem's uint8 gather."""
         self.dev, self.studies, self.slices, self.flip_tta = dev, studies, slices, flip_tta
+        self.zoom = None if zoom is None or tuple(zoom) == (1.0, 0.0, 0.0) else tuple(float(z) for z in zoom)
         self.n_win = slices - DEPTH + 1
         self.per_view = self.n_win * (2 if flip_tta else 1)
         self.n_img = studies * self.per_view
@@ -58,13 +62,17 @@ class StudyRunner:
         self.logits = [torch.zeros((self.n_img, self.n_out), dtype=torch.float32, device=d) for _ in packs]
         self.views = [torch.zeros((studies, self.n_out), dtype=torch.float32, device=d) for _ in packs]
         self.out = torch.zeros((studies, self.n_out), dtype=torch.float32, device=d)
+        self.zbuf = None
+        if self.zoom is not None:
+            img = int(self.encoders[0].in_shape[2])
+            self.zbuf = torch.empty((self.n_img, 3, img, img), dtype=torch.float16, device=d)
 
     @property
     def launches_per_call(self) -> int:
         per_pass = 2 + 2 * sum(b["L"] for b in self.encoders[0].meta["blocks"]) + \
             sum(1 for b in self.encoders[0].meta["blocks"] if b["trans"])
         passes = -(-self.n_img // self.encoders[0].nb)
-        return per_pass * passes * len(self.encoders)
+        return (per_pass * passes + (1 if self.zoom is not None else 0)) * len(self.encoders)
 
     def run(self, volumes: torch.Tensor) -> torch.Tensor:
         """Study logits [studies, n_out] (the mean over seeds of each seed's view mean)."""
@@ -74,7 +82,13 @@ class StudyRunner:
                              f"[windows, {self.studies}, slices, H, W]")
         for k, enc in enumerate(self.encoders):
             planes = volumes[k % nwin].reshape(-1, volumes.shape[-2], volumes.shape[-1])
-            enc.encode_u8(planes, self.src, self.flags, self.logits[k], self.views[k], self.per_view)
+            if self.zoom is None:
+                enc.encode_u8(planes, self.src, self.flags, self.logits[k], self.views[k], self.per_view)
+            else:
+                from . import ops
+                h, w = planes.shape[-2], planes.shape[-1]
+                ops.zoom(planes, self.src, self.zbuf, self.n_img, h, w, *self.zoom, flags=self.flags)
+                enc.encode(self.zbuf, self.logits[k], self.views[k], self.per_view)
         torch.mean(torch.stack(self.views), 0, out=self.out)
         return self.out
 

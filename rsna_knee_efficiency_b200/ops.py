@@ -63,6 +63,14 @@ def head(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: in
     nat.check(nat.lib().dn8_head(a, _stream(stream)), "dn8_head")
 
 
+def zoom(planes: torch.Tensor, src: torch.Tensor, out: torch.Tensor, N: int, H: int, W: int,
+         scale: float, tx: float = 0.0, ty: float = 0.0, flags: torch.Tensor | None = None,
+         err: torch.Tensor | None = None, stream=None) -> None:
+    """Zoomed / shifted fp16 windows [N, 3, H, W] from uint8 planes [P, H, W] (src int32 [N, 4])."""
+    a = nat.ZoomArgs(_ptr(planes), _ptr(src), _ptr(flags), _ptr(out), _ptr(err), N, H, W, scale, tx, ty)
+    nat.check(nat.lib().dn8_zoom(a, _stream(stream)), "dn8_zoom")
+
+
 def head_noalloc(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: int, N: int, HW: int,
                  feat: torch.Tensor | None = None, hw: torch.Tensor | None = None, hb: torch.Tensor | None = None,
                  logits: torch.Tensor | None = None, view_logits: torch.Tensor | None = None,

@@ -143,3 +143,13 @@ def test_kernel_entry_points_reject_bad_geometry_without_launching():
     assert lib.dn8_stem(ctypes.byref(s), None) == nat.DN8_EINVAL
     assert lib.dn8_conv1(None, None) == nat.DN8_EINVAL
     assert lib.dn8_last_error()
+
+
+def test_zoom_rejects_bad_arguments_without_launching():
+    lib = nat.lib()
+    fake = 1 << 20
+    a = nat.ZoomArgs(fake, fake, None, fake, None, 2, 64, 72, 1.1, 0.0, 0.0)       # W % 16 != 0
+    assert lib.dn8_zoom(ctypes.byref(a), None) == nat.DN8_EINVAL
+    a.W, a.scale = 64, 0.2                                                          # scale < 0.25
+    assert lib.dn8_zoom(ctypes.byref(a), None) == nat.DN8_EINVAL
+    assert b"dn8_zoom" in lib.dn8_last_error()
