@@ -467,19 +467,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int chunk = tile % nch;
             const int m = (tile / nch) * 128 + quad * 32 + lane;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
-            // requantise 32 columns (output channels c0 ..) of this warp's 32 rows and store them
-            auto finish = [&](const uint32_t (&v)[32], int cb) {
+            // requantise 16 columns (output channels c0 ..) of this warp's 32 rows and store them
+            auto finish = [&](const uint32_t (&v)[16], int cb) {
                 const int c0 = chunk * NC + half * ncol + cb;      // first output channel (even)
                 const float4* gdp = gd4 + (c0 >> 1);               // (g, d) pairs of channels c0 ..
-                uint32_t wd[8];
+                uint32_t wd[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < 4; ++j) {
                     uint32_t b[4];
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int c = 4 * j + 2 * e;
-                        // scalar ops with immediate constants: packed pairs of constants would cost
-                        // register moves
                         float f0, f1;
                         if (fast_cvt) {
                             f0 = __uint_as_float(v[c]) - ACC_MAGIC_F;
@@ -503,28 +501,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     wd[j] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
                 }
                 if (m < rows) {
-                    if (TRANS) {
-                        // next block input, group-major [c_out / 32][N * HW / 4][32]
-                        int8_t* o = static_cast<int8_t*>(a.out) + (static_cast<size_t>(c0 >> 5) * rows + m) * 32;
-                        *reinterpret_cast<uint4*>(o) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-                        *reinterpret_cast<uint4*>(o + 16) = make_uint4(wd[4], wd[5], wd[6], wd[7]);
-                    } else {
-                        uint8_t* o = static_cast<uint8_t*>(a.out);
-                        const int plane = c0 >> 4;
-                        *reinterpret_cast<uint4*>(o + (static_cast<size_t>(plane) * rows + m) * 16) =
-                            make_uint4(wd[0], wd[1], wd[2], wd[3]);
-                        *reinterpret_cast<uint4*>(o + (static_cast<size_t>(plane + 1) * rows + m) * 16) =
-                            make_uint4(wd[4], wd[5], wd[6], wd[7]);
-                    }
+                    uint8_t* o = static_cast<uint8_t*>(a.out);
+                    // transition: next block input, group-major [c_out / 32][N * HW / 4][32];
+                    // conv1: bottleneck planes of 16 channels [8][N * HW][16]
+                    const size_t off = TRANS ? (static_cast<size_t>(c0 >> 5) * rows + m) * 32 + (c0 & 16)
+                                             : (static_cast<size_t>(c0 >> 4) * rows + m) * 16;
+                    *reinterpret_cast<uint4*>(o + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
                 }
             };
+            // 16-column chunks, each chunk's TMEM load issued one chunk ahead (tcgen05.wait::ld waits
+            // for every earlier load, so the load of chunk k + 1 is in flight while chunk k is worked)
+            uint32_t va[16], vb[16];
+            tmem_ld16(taddr, va);
             for (int cb = 0; cb < ncol; cb += 32) {
-                uint32_t v[32];
-                tmem_ld32(taddr + cb, v);
                 tmem_wait_ld();
-                tmem_fill32(taddr + cb, ACC_MAGIC);                 // re-arm for the tile after next
-                finish(v, cb);
+                tmem_ld16(taddr + cb + 16, vb);
+                finish(va, cb);
+                tmem_wait_ld();
+                if (cb + 32 < ncol) tmem_ld16(taddr + cb + 32, va);
+                finish(vb, cb + 16);
             }
+            for (int cb = 0; cb < ncol; cb += 32) tmem_fill32(taddr + cb, ACC_MAGIC);   // re-arm
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
