@@ -197,8 +197,9 @@ DN8_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 DN8_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 #undef DN8_R8
 
-// Accumulators start at ACC_MAGIC (the bits of the float 1.5 * 2^23): MAGIC + acc read as a float is
-// 1.5 * 2^23 + acc exactly while |acc| < 2^22, so (float)acc is one subtraction.
+// ACC_MAGIC = the bits of the float 1.5 * 2^23: the int32 MAGIC + acc (an accumulator armed with MAGIC,
+// or an integer add) read as a float is 1.5 * 2^23 + acc exactly while |acc| < 2^22, so (float)acc
+// is one subtraction.
 constexpr uint32_t ACC_MAGIC = 0x4B400000u;
 constexpr float ACC_MAGIC_F = 12582912.0f;
 

@@ -173,16 +173,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    if (warp >= 11) {                                  // arm both accumulators with MAGIC
-        uint32_t arm[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
-        const int quad = warp & 3, half = (warp - 11) >> 2;
-        for (int acc = 0; acc < 2; ++acc)
-            for (int cb = 0; cb < (NC >> 1); cb += 32)
-                tmem_st32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * (NC >> 1) + cb, arm);
-        tmem_wait_st();
-    }
     tc_fence_before();
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
@@ -226,12 +216,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                         // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
                         if (TRANS || x < gc) {
                             const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
+                            const uint32_t accum = (j | x) ? 1u : 0u;   // the tile's first MMA overwrites
                             if constexpr (TMEM_A) {
                                 umma_u8s8_ts(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
-                                             idesc, 1u);                         // accumulators start at MAGIC
+                                             idesc, accum);
                             } else {
                                 const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
-                                umma_u8s8(tmem + acc * NC, ad, bd, idesc, 1u);
+                                umma_u8s8(tmem + acc * NC, ad, bd, idesc, accum);
                             }
                         }
                     }
@@ -453,8 +444,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         }
     } else {
         // ---------------- epilogue ----------------
-        // TMEM accumulators hold MAGIC + acc (they are re-armed with MAGIC after every read, and
-        // every MMA accumulates), so the int -> float conversion is one packed subtraction.
+        // TMEM accumulators hold the int32 sums (each tile's first MMA overwrites); the int -> float
+        // conversion is an integer add of the MAGIC bits and one float subtraction.
         const int quad = warp & 3, half = (warp - 11) >> 2;
         const int ncol = NC >> 1;                              // columns of this warp
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
@@ -480,11 +471,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                         const int c = 4 * j + 2 * e;
                         float f0, f1;
                         if (fast_cvt) {
-                            f0 = __uint_as_float(v[c]) - ACC_MAGIC_F;
-                            f1 = __uint_as_float(v[c + 1]) - ACC_MAGIC_F;
+                            f0 = __uint_as_float(v[c] + ACC_MAGIC) - ACC_MAGIC_F;
+                            f1 = __uint_as_float(v[c + 1] + ACC_MAGIC) - ACC_MAGIC_F;
                         } else {
-                            f0 = __int2float_rn(static_cast<int32_t>(v[c] - ACC_MAGIC));
-                            f1 = __int2float_rn(static_cast<int32_t>(v[c + 1] - ACC_MAGIC));
+                            f0 = __int2float_rn(static_cast<int32_t>(v[c]));
+                            f1 = __int2float_rn(static_cast<int32_t>(v[c + 1]));
                         }
                         const float4 p = gdp[c >> 1];                  // (g, d) of channels c0+c, c0+c+1
                         float r0, r1;
@@ -521,8 +512,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 if (cb + 32 < ncol) tmem_ld16(taddr + cb + 32, va);
                 finish(vb, cb + 16);
             }
-            for (int cb = 0; cb < ncol; cb += 32) tmem_fill32(taddr + cb, ACC_MAGIC);   // re-arm
-            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[acc]);
