@@ -166,7 +166,9 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             tmem_ld16(taddr, d0);
             tmem_ld16(taddr + 32, d1);
             tmem_ld16(taddr + 64, d2);
-            tmem_wait_ld();
+            tmem_wait_ld(d0);
+            reg_bind(d1);
+            reg_bind(d2);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[acc]);

@@ -153,7 +153,21 @@ DN8_DEV void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(smem_u32(bar)) : "memory");
 }
-DN8_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.ld writes its registers asynchronously: their values may be read only after
+// tcgen05.wait::ld. A wait with a "memory" clobber alone orders memory, not registers, so the compiler
+// could schedule arithmetic on the loaded registers above it. The waits below name the registers of
+// the outstanding loads as in/out operands, so every use depends on the wait; reg_bind extends that
+// to more registers after a wait (an empty asm, ordered after the wait as both are volatile).
+#define DN8_B8(i) "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), \
+                  "+r"(r[i + 4]), "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7])
+DN8_DEV void tmem_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : DN8_B8(0), DN8_B8(8) : : "memory");
+}
+DN8_DEV void tmem_wait_ld(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : DN8_B8(0), DN8_B8(8), DN8_B8(16), DN8_B8(24) : : "memory");
+}
+DN8_DEV void reg_bind(uint32_t (&r)[16]) { asm volatile("" : DN8_B8(0), DN8_B8(8) : : "memory"); }
+#undef DN8_B8
 
 #define DN8_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \
                   "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])

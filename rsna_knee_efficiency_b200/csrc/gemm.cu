@@ -505,10 +505,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             uint32_t va[16], vb[16];
             tmem_ld16(taddr, va);
             for (int cb = 0; cb < ncol; cb += 32) {
-                tmem_wait_ld();
+                tmem_wait_ld(va);
                 tmem_ld16(taddr + cb + 16, vb);
                 finish(va, cb);
-                tmem_wait_ld();
+                tmem_wait_ld(vb);
                 if (cb + 32 < ncol) tmem_ld16(taddr + cb + 32, va);
                 finish(vb, cb + 16);
             }

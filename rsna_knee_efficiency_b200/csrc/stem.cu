@@ -112,16 +112,6 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-    if (warp >= 5) {                                      // arm both accumulators with MAGIC
-        uint32_t arm[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
-        const int quad = warp & 3, hc = (warp - 5) >> 2;
-        for (int acc = 0; acc < 2; ++acc)
-            for (int m = 0; m < MT; ++m)
-                tmem_st32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * 128 + m * 64 + hc * 32, arm);
-        tmem_wait_st();
-    }
     tc_fence_before();
     const int fast_cvt = __syncthreads_and(ok);
     tc_fence_after();
@@ -161,7 +151,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         for (int kk = 0; kk < ST_KSTEPS; ++kk) {
                             const uint64_t ad = sdesc(a0 + ((b * MT + m) * ST_KSTEPS + kk) * 4096, 16, 256, LAYOUT_SW32);
                             const uint64_t bd = sdesc(w0 + kk * 2048, 16, 256, LAYOUT_SW32);
-                            umma_u8s8(tmem + b * 128 + m * 64, ad, bd, idesc, 1u);
+                            umma_u8s8(tmem + b * 128 + m * 64, ad, bd, idesc, kk ? 1u : 0u);   // first overwrites
                         }
                     umma_commit(&emptyA[b]);
                     umma_commit(&accf[b]);
@@ -300,9 +290,6 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         const int et = threadIdx.x - 160;                 // 0..255
         const int pxh = et & 1, px0 = et >> 1;            // pooling: channel half, first pooled pixel
         const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
-        uint32_t arm[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) arm[j] = ACC_MAGIC;
         int i = 0;
         for (int t = 0; t < my_tasks; ++t) {
             int n, py0, cr0, nrows;
@@ -322,8 +309,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                     uint32_t v[32];
                     const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 128 + m * 64 + hc * 32;
                     tmem_ld32(taddr, v);
-                    tmem_wait_ld();
-                    tmem_st32(taddr, arm);
+                    tmem_wait_ld(v);
                     uint32_t wd[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
@@ -334,8 +320,8 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         float f[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
-                            f[e] = fast_cvt ? __uint_as_float(v[4 * j + e]) - ACC_MAGIC_F
-                                            : __int2float_rn(static_cast<int32_t>(v[4 * j + e] - ACC_MAGIC));
+                            f[e] = fast_cvt ? __uint_as_float(v[4 * j + e] + ACC_MAGIC) - ACC_MAGIC_F
+                                            : __int2float_rn(static_cast<int32_t>(v[4 * j + e]));
                         float tq[4];
                         f2_unpack(f2_fma(f2_pack(f[0], f[1]), f2_pack(k4.x, k4.y), f2_pack(c4.x, c4.y)), tq[0], tq[1]);
                         f2_unpack(f2_fma(f2_pack(f[2], f[3]), f2_pack(k4.z, k4.w), f2_pack(c4.z, c4.w)), tq[2], tq[3]);
@@ -355,7 +341,6 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                                 make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]);
                     }
                 }
-                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
