@@ -185,11 +185,6 @@ DN8_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
                  : DN8_R8(0), DN8_R8(8)
                  : "r"(taddr) : "memory");
 }
-DN8_DEV void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
-                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
-                   "r"(r[7]) : "memory");
-}
 // 32 consecutive columns of the warp's 32 lanes set to one value (one register for all 32 operands).
 DN8_DEV void tmem_fill32(uint32_t taddr, uint32_t v) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -209,6 +204,17 @@ DN8_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
                  : "memory");
 }
 DN8_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// tcgen05.st reads its source registers asynchronously: they must keep their values until
+// tcgen05.wait::st. This wait names them as inputs, so the compiler keeps them live (and does not
+// reuse them) until the stores have completed.
+DN8_DEV void tmem_wait_st(const uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::st.sync.aligned;"
+                 ::"r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+                   "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+                   "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+                   "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+                 : "memory");
+}
 #undef DN8_R8
 
 // ACC_MAGIC = the bits of the float 1.5 * 2^23: the int32 MAGIC + acc (an accumulator armed with MAGIC,

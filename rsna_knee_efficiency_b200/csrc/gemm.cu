@@ -311,50 +311,56 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
             if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
             tc_fence_after();
-            // one unit (K group) at a time: 32 raw bytes -> 8 prologue words -> 8 TMEM columns
+            // the stage's units (K groups): 32 raw bytes each -> 8 prologue words; all 4 units (32
+            // TMEM columns) in one store, whose registers stay live until tcgen05.wait::st
+            uint32_t res[32];
 #pragma unroll
             for (int x = 0; x < UNITS; ++x) {
-                if (x >= gc) break;
+                uint32_t* rx = res + 8 * x;
+                if (x >= gc) {                                // short last stage: columns never read
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) rx[k] = 0u;
+                    continue;
+                }
                 const int g = j_this * KSTEP + x;
                 // (2-way bank conflicts on these two reads cost less than swapping the halves)
                 const uint8_t* src = sR + s * RB + x * 4096 + r * 32;
                 const uint4 lo = *reinterpret_cast<const uint4*>(src);
                 const uint4 hi = *reinterpret_cast<const uint4*>(src + 16);
-                uint32_t res[8];
                 if (F16) {
                     const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128);   // 32 channels
                     uint4 tt = tb[0];
-                    res[0] = prologue_f16x4(lo.x, tt.x, tt.y, tt.z, tt.w);
+                    rx[0] = prologue_f16x4(lo.x, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[1];
-                    res[1] = prologue_f16x4(lo.y, tt.x, tt.y, tt.z, tt.w);
+                    rx[1] = prologue_f16x4(lo.y, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[2];
-                    res[2] = prologue_f16x4(lo.z, tt.x, tt.y, tt.z, tt.w);
+                    rx[2] = prologue_f16x4(lo.z, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[3];
-                    res[3] = prologue_f16x4(lo.w, tt.x, tt.y, tt.z, tt.w);
+                    rx[3] = prologue_f16x4(lo.w, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[4];
-                    res[4] = prologue_f16x4(hi.x, tt.x, tt.y, tt.z, tt.w);
+                    rx[4] = prologue_f16x4(hi.x, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[5];
-                    res[5] = prologue_f16x4(hi.y, tt.x, tt.y, tt.z, tt.w);
+                    rx[5] = prologue_f16x4(hi.y, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[6];
-                    res[6] = prologue_f16x4(hi.z, tt.x, tt.y, tt.z, tt.w);
+                    rx[6] = prologue_f16x4(hi.z, tt.x, tt.y, tt.z, tt.w);
                     tt = tb[7];
-                    res[7] = prologue_f16x4(hi.w, tt.x, tt.y, tt.z, tt.w);
+                    rx[7] = prologue_f16x4(hi.w, tt.x, tt.y, tt.z, tt.w);
                 } else {
                     const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32;
-                    res[0] = prologue_f32x4(lo.x, tb);
-                    res[1] = prologue_f32x4(lo.y, tb + 4);
-                    res[2] = prologue_f32x4(lo.z, tb + 8);
-                    res[3] = prologue_f32x4(lo.w, tb + 12);
-                    res[4] = prologue_f32x4(hi.x, tb + 16);
-                    res[5] = prologue_f32x4(hi.y, tb + 20);
-                    res[6] = prologue_f32x4(hi.z, tb + 24);
-                    res[7] = prologue_f32x4(hi.w, tb + 28);
+                    rx[0] = prologue_f32x4(lo.x, tb);
+                    rx[1] = prologue_f32x4(lo.y, tb + 4);
+                    rx[2] = prologue_f32x4(lo.z, tb + 8);
+                    rx[3] = prologue_f32x4(lo.w, tb + 12);
+                    rx[4] = prologue_f32x4(hi.x, tb + 16);
+                    rx[5] = prologue_f32x4(hi.y, tb + 20);
+                    rx[6] = prologue_f32x4(hi.z, tb + 24);
+                    rx[7] = prologue_f32x4(hi.w, tb + 28);
                 }
-                tmem_st8(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8) + x * 8, res);
             }
+            tmem_st32(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8), res);
             __syncwarp();
             if (lane == 0) mbar_arrive(&freeR[s]);
-            tmem_wait_st();
+            tmem_wait_st(res);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&fullA[sa]);
