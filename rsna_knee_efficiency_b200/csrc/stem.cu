@@ -352,9 +352,11 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 if ((cr & 1) == 1 && py >= py0) {
                     if (!mbar_wait(&written[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
                     for (int px = px0; px < PW; px += 128) {
-                        uint32_t mx[8];
+                        // per-byte max of the 9 taps as u16x2 max of the even and the odd bytes of
+                        // every word (one native instruction each; a 4-byte SIMD max is not native)
+                        uint32_t mxe[8], mxo[8];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) mx[j] = 0u;
+                        for (int j = 0; j < 8; ++j) mxe[j] = mxo[j] = 0u;
 #pragma unroll
                         for (int dy = -1; dy <= 1; ++dy) {
                             const int cyy = 2 * py + dy;
@@ -370,16 +372,21 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
 #pragma unroll
                                 for (int j = 0; j < 2; ++j) {
                                     const uint4 q = *reinterpret_cast<const uint4*>(pp + (((2 * pxh + j) ^ (trow & 3)) << 4));
-                                    mx[4 * j] = __vmaxu4(mx[4 * j], q.x);
-                                    mx[4 * j + 1] = __vmaxu4(mx[4 * j + 1], q.y);
-                                    mx[4 * j + 2] = __vmaxu4(mx[4 * j + 2], q.z);
-                                    mx[4 * j + 3] = __vmaxu4(mx[4 * j + 3], q.w);
+                                    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                                    for (int k = 0; k < 4; ++k) {
+                                        mxe[4 * j + k] = __vmaxu2(mxe[4 * j + k], __byte_perm(qw[k], 0u, 0x4240));
+                                        mxo[4 * j + k] = __vmaxu2(mxo[4 * j + k], __byte_perm(qw[k], 0u, 0x4341));
+                                    }
                                 }
                             }
                         }
                         // block 1 input, group-major [2][N][PH * PW][32]: this half is group pxh
                         const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
                         int8_t* o = a.out + pxh * gstride + pix * 32;
+                        uint32_t mx[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) mx[j] = __byte_perm(mxe[j], mxo[j], 0x6240);
                         *reinterpret_cast<uint4*>(o) = make_uint4(mx[0], mx[1], mx[2], mx[3]);
                         *reinterpret_cast<uint4*>(o + 16) = make_uint4(mx[4], mx[5], mx[6], mx[7]);
                     }
