@@ -125,12 +125,15 @@ int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out) {
 int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out) {
     if (tw == nullptr || out == nullptr || G < 1 || cout < 128 || cout % 128)
         return fail(DN8_EINVAL, "dn8_prepare_trans_weights: bad arguments");
-    const int nc = dn8::trans_chunk(cout), nchunks = cout / nc;
-    // [nchunks][G][nc rows][32]: chunk c holds output channels c * nc .. c * nc + nc - 1
-    for (int c = 0; c < nchunks; ++c)
+    const int nc = dn8::trans_chunk(cout), nchunks = (cout + nc - 1) / nc;
+    // [nchunks][G][w rows][32]: chunk c holds output channels c * nc .. c * nc + w - 1,
+    // w = min(nc, cout - c * nc), and starts at byte G * 32 * c * nc
+    for (int c = 0; c < nchunks; ++c) {
+        const int w = cout - c * nc < nc ? cout - c * nc : nc;
         for (int g = 0; g < G; ++g)
-            swizzle32_tile(tw + (static_cast<size_t>(g) * cout + static_cast<size_t>(c) * nc) * 32, nc,
-                           out + (static_cast<size_t>(c) * G + g) * nc * 32);
+            swizzle32_tile(tw + (static_cast<size_t>(g) * cout + static_cast<size_t>(c) * nc) * 32, w,
+                           out + static_cast<size_t>(G) * 32 * c * nc + static_cast<size_t>(g) * w * 32);
+    }
     return DN8_OK;
 }
 

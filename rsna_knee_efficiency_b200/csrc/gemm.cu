@@ -51,14 +51,14 @@ constexpr int UNITS = 4;
 struct GemmArgs {
     const int8_t* in0;        // block input groups [G0][N][HW][32]
     const int8_t* seg;        // layer segments [L][N][HW][32]
-    const uint8_t* wu;        // UMMA-ready weights [nchunks][G][NC rows x 32 B, 32B-swizzled]
+    const uint8_t* wu;        // UMMA-ready weights [nchunks][G][chunk rows x 32 B, 32B-swizzled]
     const void* ab;           // prologue table (fp16 pairs or fp32 pairs)
     const float* gd;          // epilogue table [cout][2]
     void* out;
     int* err;
     int G0, G, N, HW, W;      // W: image width (transition)
     int rows;                 // GEMM rows: N*HW (conv1) or N*HW/4 (transition)
-    int cout, nc, nchunks;    // output channels, channels per chunk, chunks
+    int cout, nc, nchunks;    // output channels, channels per chunk (the last one may be 128), chunks
     int b_resident;           // 1: all G weight tiles stay in shared memory
     int sb;                   // weight ring stages when streamed
     int raw_bytes;            // raw ring slot size (a whole stage)
@@ -187,13 +187,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     if (warp == 0) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = idesc_u8s8(128, NC);
             const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
             bool ok_run = true;
             if (a.b_resident && T > 0) ok_run = mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
             int i = 0;
             for (int t = 0; t < my_tiles && ok_run; ++t) {
                 const int acc = t & 1;
+                const int chunk = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) % a.nchunks;
+                const uint32_t idesc = idesc_u8s8(128, min(NC, a.cout - chunk * NC));   // chunk width
                 if (!mbar_wait(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
                 tc_fence_after();
                 for (int j = 0; j < NS; ++j, ++i) {
@@ -277,15 +278,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 for (int t = 0; t < my_tiles; ++t) {
                     const int tile = blockIdx.x + t * gridDim.x;
                     const int chunk = tile % a.nchunks;
+                    const int cbt = min(NC, a.cout - chunk * NC) * 32;      // weight tile bytes of the chunk
+                    const uint8_t* wc = a.wu + static_cast<size_t>(G) * 32 * chunk * NC;
                     bool ok_run = true;
                     for (int j = 0; j < NS; ++j, ++i) {
                         const int s = i % a.sb;
                         const int gc = min(KSTEP, G - j * KSTEP);
                         if (!mbar_wait(&emptyB[s], ((i / a.sb) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
                         // the gc weight tiles of the stage are contiguous in the prepared table
-                        mbar_expect_tx(&fullB[s], static_cast<uint32_t>(gc * btile));
-                        bulk_g2s(sB + s * bstage, a.wu + (static_cast<size_t>(chunk) * G + j * KSTEP) * btile,
-                                 static_cast<uint32_t>(gc * btile), &fullB[s]);
+                        mbar_expect_tx(&fullB[s], static_cast<uint32_t>(gc * cbt));
+                        bulk_g2s(sB + s * bstage, wc + static_cast<size_t>(j) * KSTEP * cbt,
+                                 static_cast<uint32_t>(gc * cbt), &fullB[s]);
                     }
                     if (!ok_run) break;
                 }
@@ -453,7 +456,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         // TMEM accumulators hold the int32 sums (each tile's first MMA overwrites); the int -> float
         // conversion is an integer add of the MAGIC bits and one float subtraction.
         const int quad = warp & 3, half = (warp - 11) >> 2;
-        const int ncol = NC >> 1;                              // columns of this warp
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
         for (int t = 0; t < my_tiles; ++t) {
             const int acc = t & 1;
@@ -462,6 +464,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int tile = blockIdx.x + t * gridDim.x;
             const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
             const int chunk = tile % nch;
+            const int ncol = min(NC, a.cout - chunk * NC) >> 1;      // columns of this warp
             const int m = (tile / nch) * 128 + quad * 32 + lane;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
             // requantise 16 columns (output channels c0 ..) of this warp's 32 rows and store them
@@ -555,8 +558,9 @@ cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool
     return a.prologue_f16 ? launch_gemm<true, false>(g, sms, st, pdl) : launch_gemm<false, false>(g, sms, st, pdl);
 }
 
-// output channels per CTA tile: 256 when it divides c_out (TMEM: 2 x 256 columns), else 128
-int trans_chunk(int cout) { return cout % 256 == 0 ? 256 : 128; }
+// output channels per CTA tile: 256 (TMEM: 2 x 256 columns; the last chunk of a c_out that is an
+// odd multiple of 128 has 128), or 128 when c_out is 128
+int trans_chunk(int cout) { return cout >= 256 ? 256 : 128; }
 
 // Largest raw span of a transition tile: its 128 consecutive pooled pixels cover at most
 // 128 / W2 pooled rows when W2 divides 128 (tiles start on a row), else ceil(128 / W2) + 1;
@@ -573,7 +577,8 @@ cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st, bool
     g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
     g.out = a.out; g.err = a.err;
     g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.H * a.W; g.W = a.W;
-    g.rows = a.N * (a.H / 2) * (a.W / 2); g.cout = cout; g.nc = trans_chunk(cout); g.nchunks = cout / g.nc;
+    g.rows = a.N * (a.H / 2) * (a.W / 2); g.cout = cout; g.nc = trans_chunk(cout);
+    g.nchunks = (cout + g.nc - 1) / g.nc;
     g.raw_bytes = trans_raw_bytes(a.W);
     return a.prologue_f16 ? launch_gemm<true, true>(g, sms, st, pdl) : launch_gemm<false, true>(g, sms, st, pdl);
 }

@@ -102,8 +102,9 @@ def test_prepare_trans_weights(G, cout):
     tw = rng.integers(-127, 128, size=(G, cout, 32), dtype=np.int64).astype(np.int8)
     out = np.zeros(G * cout * 32, np.uint8)
     assert _call(nat.lib().dn8_prepare_trans_weights, tw, G, cout, out) == nat.DN8_OK
-    nc = 256 if cout % 256 == 0 else 128
-    parts = [_swz32(tw[g, c * nc:(c + 1) * nc]) for c in range(cout // nc) for g in range(G)]
+    # chunks of 256 output channels, the last one 128 when c_out is an odd multiple of 128
+    nc = 256 if cout >= 256 else 128
+    parts = [_swz32(tw[g, c * nc:min(cout, (c + 1) * nc)]) for c in range(-(-cout // nc)) for g in range(G)]
     np.testing.assert_array_equal(out, np.concatenate(parts).view(np.uint8).reshape(-1))
     assert _call(nat.lib().dn8_prepare_trans_weights, tw, G, 96, out) == nat.DN8_EINVAL
 
