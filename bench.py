@@ -232,10 +232,14 @@ def roofline(enc, runner, hbm_gbs: float, i8_tops: float, peak_kind: str, vol_de
             k[3] += 1
     c1 = per["conv1"]
     achieved = c1[0] / (c1[1] * 1e-3) / 1e9
+    # DRAM traffic of conv1 over one pass from an ncu capture (profiles/), scaled to this pass size
+    # (traffic grows with the images of a pass: every launch streams its layer's activations)
     traffic = None
-    tf = ROOT / "profiles" / "dram_traffic_encoder_512_b192.json"
+    tf = ROOT / "profiles" / "dram_traffic_encoder_512_b384.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("conv1_dram_bytes_per_pass")
+        t = json.loads(tf.read_text())
+        if t.get("conv1_dram_bytes_per_pass") and t.get("pass_images"):
+            traffic = int(t["conv1_dram_bytes_per_pass"] * n / t["pass_images"])
     summary = {k: {"launches": v[3], "ms": round(v[1], 3), "GBps": round(v[0] / (v[1] * 1e-3) / 1e9, 1),
                    "roof_ms": round(v[2], 4), "frac": round(v[2] / v[1], 3)} for k, v in per.items()}
     kinds = [v for k, v in per.items() if "." not in k]
