@@ -146,16 +146,26 @@ class Dense8SEncoder:
         """Encode n = len(src) images gathered from uint8 planes [P, img, img] (src int32 [n, 4] =
         plane of each channel, flags int32 [n] bit 0 = horizontal flip). Fills `logits` [n, n_out]
         and `views` [n / per_view, n_out] when given. Returns out[:n] (features)."""
+        cur = torch.cuda.current_stream(self.dev)
+        self.stream.wait_stream(cur)
+        out = self.enqueue_u8(planes, src, flags, logits, views, per_view)
+        cur.wait_stream(self.stream)
+        return out
+
+    def enqueue_u8(self, planes: torch.Tensor, src: torch.Tensor, flags: torch.Tensor | None = None,
+                   logits: torch.Tensor | None = None, views: torch.Tensor | None = None,
+                   per_view: int = 0) -> torch.Tensor:
+        """`encode_u8` without the stream hand-offs: the pass is enqueued on the encoder's own
+        stream (`self.stream`) only. The caller makes that stream wait for the inputs and waits on it
+        before reading the outputs; this lets several encoders (the seeds of a study batch) run
+        their passes concurrently."""
         n = src.shape[0]
         if planes.dtype != torch.uint8 or src.dtype != torch.int32:
             raise ValueError("encode_u8: uint8 planes and int32 plane table expected")
-        cur = torch.cuda.current_stream(self.dev)
-        self.stream.wait_stream(cur)
         with torch.cuda.stream(self.stream):
             inp = nat.Input(planes.data_ptr(), src.data_ptr(), None if flags is None else flags.data_ptr(), 1)
             self._forward(inp, n, self.out.data_ptr(), None if logits is None else logits.data_ptr(),
                           None if views is None else views.data_ptr(), per_view)
-        cur.wait_stream(self.stream)
         return self.out[:n]
 
     def encode(self, x: torch.Tensor, logits: torch.Tensor | None = None, views: torch.Tensor | None = None,

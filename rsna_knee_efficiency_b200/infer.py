@@ -80,12 +80,23 @@ class StudyRunner:
         if S != self.studies or volumes.dtype != torch.uint8:
             raise ValueError(f"volumes {tuple(volumes.shape)} {volumes.dtype}: expected uint8 "
                              f"[windows, {self.studies}, slices, H, W]")
-        for k, enc in enumerate(self.encoders):
-            planes = volumes[k % nwin].reshape(-1, volumes.shape[-2], volumes.shape[-1])
-            if self.zoom is None:
-                enc.encode_u8(planes, self.src, self.flags, self.logits[k], self.views[k], self.per_view)
-            else:
-                from . import ops
+        if self.zoom is None:
+            # the seeds' passes are independent (own engines, buffers and streams): both start
+            # after the caller's stream and run concurrently, so one seed's kernels fill the SMs
+            # the other's leave idle at the end of a launch
+            cur = torch.cuda.current_stream(self.encoders[0].dev)
+            for enc in self.encoders:
+                enc.stream.wait_stream(cur)
+            for k, enc in enumerate(self.encoders):
+                planes = volumes[k % nwin].reshape(-1, volumes.shape[-2], volumes.shape[-1])
+                enc.enqueue_u8(planes, self.src, self.flags, self.logits[k], self.views[k], self.per_view)
+            for enc in self.encoders:
+                cur.wait_stream(enc.stream)
+        else:
+            # one zoom buffer serves every seed in turn
+            from . import ops
+            for k, enc in enumerate(self.encoders):
+                planes = volumes[k % nwin].reshape(-1, volumes.shape[-2], volumes.shape[-1])
                 h, w = planes.shape[-2], planes.shape[-1]
                 ops.zoom(planes, self.src, self.zbuf, self.n_img, h, w, *self.zoom, flags=self.flags)
                 enc.encode(self.zbuf, self.logits[k], self.views[k], self.per_view)
