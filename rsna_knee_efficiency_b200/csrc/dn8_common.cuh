@@ -167,6 +167,9 @@ DN8_DEV void tmem_wait_ld(uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" : DN8_B8(0), DN8_B8(8), DN8_B8(16), DN8_B8(24) : : "memory");
 }
 DN8_DEV void reg_bind(uint32_t (&r)[16]) { asm volatile("" : DN8_B8(0), DN8_B8(8) : : "memory"); }
+DN8_DEV void reg_bind(uint32_t (&r)[32]) {
+    asm volatile("" : DN8_B8(0), DN8_B8(8), DN8_B8(16), DN8_B8(24) : : "memory");
+}
 #undef DN8_B8
 
 #define DN8_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \

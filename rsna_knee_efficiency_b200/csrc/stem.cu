@@ -303,44 +303,53 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 if (i > 0 && !mbar_wait(&done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
                 if (!mbar_wait(&accf[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
                 tc_fence_after();
-                for (int m = 0; m < MT; ++m) {
-                    const int row = quad * 32 + lane;              // tile row -> conv pixel (see im2col)
-                    const int cx = m * 128 + (row < 64 ? 2 * row : 2 * (row - 64) + 1);
-                    uint32_t v[32];
-                    const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 128 + m * 64 + hc * 32;
-                    tmem_ld32(taddr, v);
-                    tmem_wait_ld(v);
-                    uint32_t wd[8];
+                // both M-tiles of the conv row (MT <= 2): their TMEM loads issued together, each (k, c)
+                // quad read once for both
+                const int row = quad * 32 + lane;              // tile row -> conv pixel (see im2col)
+                const int cxr = row < 64 ? 2 * row : 2 * (row - 64) + 1;
+                const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 128 + hc * 32;
+                uint32_t v0[32], v1[32];
+                tmem_ld32(tbase, v0);
+                if (MT > 1) tmem_ld32(tbase + 64, v1);
+                tmem_wait_ld(v0);
+                reg_bind(v1);
+                // q = rint(clamp(fmaf(acc, k, c), 0, 127)) of 4 channels as the bytes of one word
+                auto requant4 = [&](const uint32_t (&v)[32], int j, const float4& k4, const float4& c4) -> uint32_t {
+                    float f[4];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        // k, c of the 4 channels (broadcast reads); fmaf pairwise in f32x2 (the k, c pairs
-                        // come straight from the float4 reads)
-                        const float4 k4 = *reinterpret_cast<const float4*>(sKC + hc * 32 + 4 * j);
-                        const float4 c4 = *reinterpret_cast<const float4*>(sKC + 64 + hc * 32 + 4 * j);
-                        float f[4];
+                    for (int e = 0; e < 4; ++e)
+                        f[e] = fast_cvt ? __uint_as_float(v[4 * j + e] + ACC_MAGIC) - ACC_MAGIC_F
+                                        : __int2float_rn(static_cast<int32_t>(v[4 * j + e]));
+                    float tq[4];
+                    f2_unpack(f2_fma(f2_pack(f[0], f[1]), f2_pack(k4.x, k4.y), f2_pack(c4.x, c4.y)), tq[0], tq[1]);
+                    f2_unpack(f2_fma(f2_pack(f[2], f[3]), f2_pack(k4.z, k4.w), f2_pack(c4.z, c4.w)), tq[2], tq[3]);
+                    uint32_t bq[4];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            f[e] = fast_cvt ? __uint_as_float(v[4 * j + e] + ACC_MAGIC) - ACC_MAGIC_F
-                                            : __int2float_rn(static_cast<int32_t>(v[4 * j + e]));
-                        float tq[4];
-                        f2_unpack(f2_fma(f2_pack(f[0], f[1]), f2_pack(k4.x, k4.y), f2_pack(c4.x, c4.y)), tq[0], tq[1]);
-                        f2_unpack(f2_fma(f2_pack(f[2], f[3]), f2_pack(k4.z, k4.w), f2_pack(c4.z, c4.w)), tq[2], tq[3]);
-                        uint32_t bq[4];
+                    for (int e = 0; e < 4; ++e)
+                        bq[e] = __float_as_uint(fminf(fmaxf(tq[e], 0.0f), 127.0f) + 12582912.0f);
+                    return __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
+                };
+                uint32_t wd0[8], wd1[8];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            bq[e] = __float_as_uint(fminf(fmaxf(tq[e], 0.0f), 127.0f) + 12582912.0f);
-                        wd[j] = __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
-                    }
-                    if (cx < CW) {
-                        // conv ring [3][MT][128 tile rows][64 B], by tile row; chunk j of row r at
-                        // (j ^ (r & 3)) spreads the banks
-                        uint8_t* cp = sC + (static_cast<size_t>(slot) * MT * 128 + m * 128 + row) * 64;
-#pragma unroll
-                        for (int j = 0; j < 2; ++j)
-                            *reinterpret_cast<uint4*>(cp + (((2 * hc + j) ^ (row & 3)) << 4)) =
-                                make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]);
-                    }
+                for (int j = 0; j < 8; ++j) {
+                    // k, c of the 4 channels (broadcast reads); fmaf pairwise in f32x2
+                    const float4 k4 = *reinterpret_cast<const float4*>(sKC + hc * 32 + 4 * j);
+                    const float4 c4 = *reinterpret_cast<const float4*>(sKC + 64 + hc * 32 + 4 * j);
+                    wd0[j] = requant4(v0, j, k4, c4);
+                    wd1[j] = MT > 1 ? requant4(v1, j, k4, c4) : 0u;
                 }
+                // conv ring [3][MT][128 tile rows][64 B], by tile row; chunk j of row r at (j ^ (r & 3))
+                // spreads the banks
+                auto put_row = [&](int m, const uint32_t (&wd)[8]) {
+                    if (m * 128 + cxr >= CW) return;
+                    uint8_t* cp = sC + (static_cast<size_t>(slot) * MT * 128 + m * 128 + row) * 64;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        *reinterpret_cast<uint4*>(cp + (((2 * hc + j) ^ (row & 3)) << 4)) =
+                            make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]);
+                };
+                put_row(0, wd0);
+                if (MT > 1) put_row(1, wd1);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
