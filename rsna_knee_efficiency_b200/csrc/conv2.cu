@@ -12,17 +12,18 @@
 // One 4-D TMA load per tile brings the 8 bottleneck planes x (Rt + 2) image rows; rows outside
 // the image arrive zero-filled (the convolution's zero padding). The weights arrive prepared
 // (dn8_prepare_conv2_weights) in one bulk copy and stay resident.
-// Warp roles: warp 0 TMEM owner + TMA producer, warp 1 MMA issuer, warps 2-9 epilogue (warp w
-// reads TMEM lanes 32*(w%4).. and 16 of the 32 outputs).
+// Warp roles: warp 0 TMEM owner + TMA producer, warp 1 MMA issuer, warps 2-17 epilogue in two
+// groups of 8 that take alternate tiles (group g: tiles t = g, g + 2, ..., accumulator g), so two
+// tiles are requantised at once; warp w reads TMEM lanes 32*(w%4).. and 16 of the 32 outputs.
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
 namespace dn8 {
 
 constexpr int C2_STAGES = 3;
-constexpr int C2_THREADS = 320;
+constexpr int C2_THREADS = 576;
 constexpr int C2_W_BYTES = 36864;            // [dy][cblk][2 halves][96 rows][16 B]
-constexpr int C2_XBUF = 3;                   // edge-exchange buffers (tile t uses t % 3)
+constexpr int C2_XBUF = 4;                   // edge-exchange buffers (tile t uses t % 4: one group's)
 
 static inline int c2_rows_per_tile(int H, int W) {
     int rt = 128 / W;
@@ -143,12 +144,12 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         __syncwarp();
     } else {
         // ---------------- epilogue ----------------
-        // Software pipeline over two tiles: iteration t loads tile t's accumulator (releasing it to
-        // the MMA at once) and publishes its edge columns, then finishes tile t - 1, whose
-        // neighbours' edges were published an iteration ago. Tile t's edges live in buffer t % 3:
-        // before writing it a warp waits for exchange t - 1, by which every warp of its channel
-        // half has finished tile t - 3 (the buffer's previous reader).
-        const int quad = warp & 3, ch = (warp - 2) >> 2;
+        // Group g = (warp - 2) / 8 takes tiles g, g + 2, ... (accumulator g). Per tile: load the
+        // accumulator (releasing it to the MMA at once), publish the edge columns, wait for the
+        // other three quads' edges (exchange t), finish. Tile t's edges live in buffer t % 4, whose
+        // previous user is tile t - 4 of the same group: before writing it, a warp has waited for
+        // exchange t - 2, by which every warp of its channel half and group has finished tile t - 4.
+        const int quad = warp & 3, ch = ((warp - 2) >> 2) & 1, grp = (warp - 2) >> 3;
         const int p = quad * 32 + lane;                       // pixel within the tile
         const int yl = p / W, x = p - yl * W;
         const bool has_l = x > 0, has_r = x < W - 1;
@@ -226,24 +227,12 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
                 *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
         };
-        auto step = [&](int t, uint32_t (&c0)[16], uint32_t (&c1)[16], uint32_t (&c2)[16],
-                        const uint32_t (&p0)[16], const uint32_t (&p1)[16], const uint32_t (&p2)[16]) -> bool {
-            if (!load(t, c0, c1, c2)) return false;
-            if (t > 0 && !wait_x(t - 1)) return false;
-            publish(t, c0, c2);
-            if (t > 0) finish(t - 1, p0, p1, p2);
-            return true;
-        };
-        uint32_t a0[16], a1[16], a2[16], b0[16], b1[16], b2[16];
-        bool ok = true;
-        for (int t = 0; t < my_tiles && ok; ++t)
-            ok = (t & 1) ? step(t, b0, b1, b2, a0, a1, a2) : step(t, a0, a1, a2, b0, b1, b2);
-        if (ok && my_tiles > 0) {
-            const int t = my_tiles - 1;
-            if (wait_x(t)) {
-                if (t & 1) finish(t, b0, b1, b2);
-                else finish(t, a0, a1, a2);
-            }
+        for (int t = grp; t < my_tiles; t += 2) {
+            uint32_t d0[16], d1[16], d2[16];
+            if (!load(t, d0, d1, d2)) break;
+            publish(t, d0, d2);
+            if (!wait_x(t)) break;
+            finish(t, d0, d1, d2);
         }
     }
 
