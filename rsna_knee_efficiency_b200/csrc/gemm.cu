@@ -19,7 +19,7 @@
 // arrive by bulk async copies into a shared-memory ring (explicit bytes in flight, no L1 staging).
 // Persistent, one CTA per SM, 19 warps:
 //   warp 0       TMEM owner and MMA issuer (lane 0).
-//   warp 1       store producer (lane 0): bulk copies into the raw ring.
+//   warp 1       store producer: bulk copies into the raw ring (one lane per K group of a stage).
 //   warp 2       weight producer (lane 0): UMMA-ready weight tiles, resident when they fit.
 //   warps 3-10   prologue: one warp per unit, raw ring -> BN/ReLU/u8 -> 32B-swizzled operands.
 //   warps 11-18  epilogue: warp w reads TMEM lanes 32*(w%4).. and half of the NC columns.
@@ -237,37 +237,41 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         __syncwarp();
     } else if (warp == 1) {
         // ---------------- store producer ----------------
-        if (lane == 0) {
-            int i = 0;
-            for (int t = 0; t < my_tiles; ++t) {
-                const int tile = blockIdx.x + t * gridDim.x;
-                const int m0 = (tile / a.nchunks) * 128;
-                const int cnt = min(128, rows - m0);
-                size_t off;
-                uint32_t bytes;
-                if (TRANS) {
-                    int first, end;
-                    trans_span(m0, cnt, HW, a.W, &first, &end);
-                    off = static_cast<size_t>(first) * 32;
-                    bytes = static_cast<uint32_t>(end - first) * 32;
-                } else {
-                    off = static_cast<size_t>(m0) * 32;
-                    bytes = static_cast<uint32_t>(cnt) * 32;
-                }
-                bool ok_run = true;
-                for (int j = 0; j < NS; ++j, ++i) {
-                    const int s = i % SR;
-                    const int gc = min(KSTEP, G - j * KSTEP);
-                    if (!mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
-                    mbar_expect_tx(&fullR[s], bytes * gc);
-                    for (int x = 0; x < gc; ++x) {                   // one copy per K group, 4 KB apart
-                        const int g = j * KSTEP + x;
-                        const int8_t* src = g < G0 ? a.in0 + g * gstride + off : a.seg + (g - G0) * gstride + off;
-                        bulk_g2s(sR + s * RB + x * (RB / KSTEP), src, bytes, &fullR[s]);
-                    }
-                }
-                if (!ok_run) break;
+        // Lane 0 waits for the slot and posts the stage's bytes; lanes 0 .. gc - 1 then each issue
+        // one K group's copy (one instruction for the whole stage).
+        int i = 0;
+        for (int t = 0; t < my_tiles; ++t) {
+            const int tile = blockIdx.x + t * gridDim.x;
+            const int m0 = (tile / a.nchunks) * 128;
+            const int cnt = min(128, rows - m0);
+            size_t off;
+            uint32_t bytes;
+            if (TRANS) {
+                int first, end;
+                trans_span(m0, cnt, HW, a.W, &first, &end);
+                off = static_cast<size_t>(first) * 32;
+                bytes = static_cast<uint32_t>(end - first) * 32;
+            } else {
+                off = static_cast<size_t>(m0) * 32;
+                bytes = static_cast<uint32_t>(cnt) * 32;
             }
+            bool ok_run = true;
+            for (int j = 0; j < NS; ++j, ++i) {
+                const int s = i % SR;
+                const int gc = min(KSTEP, G - j * KSTEP);
+                int ok = 1;
+                if (lane == 0) {
+                    ok = mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY) ? 1 : 0;
+                    if (ok) mbar_expect_tx(&fullR[s], bytes * gc);
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) { ok_run = false; break; }
+                if (lane < gc) {                                     // one copy per K group, 4 KB apart
+                    const int g = j * KSTEP + lane;
+                    const int8_t* src = g < G0 ? a.in0 + g * gstride + off : a.seg + (g - G0) * gstride + off;
+                    bulk_g2s(sR + s * RB + lane * (RB / KSTEP), src, bytes, &fullR[s]);
+                }
+            }
+            if (!ok_run) break;
         }
         __syncwarp();
     } else if (warp == 2) {
