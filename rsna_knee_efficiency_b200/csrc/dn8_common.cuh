@@ -92,9 +92,6 @@ DN8_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
-DN8_DEV void prefetch_l2_bulk(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 // 4-D tiled tensor load (no multicast) into CTA shared memory, completing on `bar`.
 DN8_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
     asm volatile(
@@ -188,13 +185,6 @@ DN8_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
                  : DN8_R8(0), DN8_R8(8)
                  : "r"(taddr) : "memory");
 }
-// 32 consecutive columns of the warp's 32 lanes set to one value (one register for all 32 operands).
-DN8_DEV void tmem_fill32(uint32_t taddr, uint32_t v) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-                 "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-                 "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};"
-                 ::"r"(taddr), "r"(v) : "memory");
-}
 DN8_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
                  "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -234,8 +224,6 @@ DN8_DEV void f2_unpack(float2 r, float& a, float& b) {
     a = r.x;
     b = r.y;
 }
-DN8_DEV float2 f2_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
-DN8_DEV float2 f2_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
 DN8_DEV float2 f2_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // ---- bit-exact prologue / epilogue arithmetic -----------------------------------------------
@@ -293,16 +281,6 @@ DN8_DEV uint32_t u8_of_f16x2(uint32_t h2) {
     const uint32_t qa = __float_as_uint(fmaf(__saturatef(a), 255.0f, 12582912.0f));
     const uint32_t qb = __float_as_uint(fmaf(__saturatef(b), 255.0f, 12582912.0f));
     return __byte_perm(qa, qb, 0x0040) & 0xFFFFu;
-}
-
-// conv1 epilogue (u8 bottleneck): rint(255 sat(fmaf(g, acc, d))) (reference :598-611).
-DN8_DEV uint32_t epi_u8(int32_t acc, float g, float d) {
-    const float v = __saturatef(fmaf(g, __int2float_rn(acc), d));
-    return __float_as_uint(fmaf(v, 255.0f, 8388608.0f)) & 0xFFu;
-}
-// Symmetric int8 requantisation rint(clamp(t, -127, 127)) as a byte (t + 1.5 * 2^23).
-DN8_DEV uint32_t q_s8(float t) {
-    return __float_as_uint(fminf(fmaxf(t, -127.0f), 127.0f) + 12582912.0f) & 0xFFu;
 }
 
 }  // namespace dn8
