@@ -105,7 +105,7 @@ typedef struct dn8_stem_args {
     const void* x;
     const int32_t* src;    /* x_u8 = 1: [N][4] plane indices */
     const int32_t* flags;  /* [N] or NULL */
-    const int8_t* w;       /* S_w8 [64][176] after dn8_prepare_stem_weights (12288 bytes) */
+    const int8_t* w;       /* S_w8 [64][176] after dn8_prepare_stem_weights (14336 bytes) */
     const float* kc;       /* S_kc [128] */
     int8_t* out;
     int32_t* err;
@@ -170,7 +170,7 @@ int dn8_zoom(const dn8_zoom_args* a, dn8_stream stream);
 int dn8_prepare_conv1_weights(const int8_t* w1, int32_t G, uint8_t* out);               /* G*4096 B */
 int dn8_prepare_trans_weights(const int8_t* tw, int32_t G, int32_t cout, uint8_t* out); /* G*cout*32 B */
 int dn8_prepare_conv2_weights(const int8_t* w2k, uint8_t* out);                         /* 36864 B */
-int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out);                           /* 12288 B */
+int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out);                           /* 14336 B */
 
 /* ---- engine level ------------------------------------------------------------------------- */
 

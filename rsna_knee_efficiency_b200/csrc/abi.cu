@@ -203,15 +203,16 @@ int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
 
 int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out) {
     if (w8 == nullptr || out == nullptr) return fail(DN8_EINVAL, "dn8_prepare_stem_weights: bad arguments");
-    // S_w8 [64][176] -> 6 K steps of [64 rows][32 B], K bytes 176 .. 191 zero, 32B-swizzled
+    // S_w8 [64][176] (k = (ch * 7 + ky) * 8 + kx') -> 7 K steps, one per kernel row ky, of
+    // [64 rows][32 B] = [ch 0 kx' 0..7 | ch 1 | ch 2 | 8 zero bytes], 32B-swizzled
     int8_t tile[64 * 32];
-    for (int kk = 0; kk < 6; ++kk) {
+    for (int ky = 0; ky < 7; ++ky) {
         for (int o = 0; o < 64; ++o)
             for (int c = 0; c < 32; ++c) {
-                const int k = kk * 32 + c;
-                tile[o * 32 + c] = k < 176 ? w8[o * 176 + k] : 0;
+                const int ch = c / 8, kx = c % 8;
+                tile[o * 32 + c] = ch < 3 ? w8[o * 176 + (ch * 7 + ky) * 8 + kx] : 0;
             }
-        swizzle32_tile(tile, 64, out + kk * 2048);
+        swizzle32_tile(tile, 64, out + ky * 2048);
     }
     return DN8_OK;
 }

@@ -189,7 +189,7 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
     const dn8_table* hb = e->n_out > 0 ? need("H_b", static_cast<size_t>(e->n_out) * 4) : nullptr;
     if (!bad.empty()) return bail(efail(e, DN8_EINVAL, "pack table %s", bad.c_str()));
     const size_t o_fab = copy_raw(fab);
-    const size_t o_sw = reserve(12288);
+    const size_t o_sw = reserve(14336);
     dn8_prepare_stem_weights(static_cast<const int8_t*>(sw8->data), stage.data() + o_sw);
     const size_t o_kc = copy_raw(skc);
     const size_t o_hw = hw ? copy_raw(hw) : 0, o_hb = hb ? copy_raw(hb) : 0;

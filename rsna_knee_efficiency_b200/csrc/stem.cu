@@ -5,17 +5,23 @@
 // Arithmetic of the reference's `stem_i8_body` (src/knee/dense8s_kernels.cu:3641-3771) and
 // `stem_q_i8` (src/knee/dense8s.py:625-643).
 //
-// K layout (the reference's `stem_weights8`, dense8s.py:532-541): k = (ch * 7 + ky) * 8 + kx',
-// kx' = kx + 1 (kx' = 0 has zero weight): 21 slots of 8 bytes; slot (ch, ky) of conv pixel cx is the
-// 8 input bytes of row 2 cy + ky - 3 starting at column 2 cx - 4. K is padded to 192 (6 MMA steps).
+// K layout: the reference's `stem_weights8` (dense8s.py:532-541) has k = (ch * 7 + ky) * 8 + kx',
+// kx' = kx + 1 (kx' = 0 has zero weight): slot (ch, ky) of conv pixel cx is the 8 input bytes of
+// row 2 cy + ky - 3 starting at column 2 cx - 4. Here the slots are regrouped by kernel row: K step
+// ky (32 bytes) = [ch 0 | ch 1 | ch 2 | 8 zero-weight bytes] of input row 2 cy + ky - 3 (7 MMA steps,
+// the same products summed in another order, exact in int32). A step depends on the input row
+// only, so the 32-byte "record" of every (input row, conv pixel) is built once and serves the
+// conv rows that read that input row (up to four).
 //
 // A CTA walks bands of BP pooled rows of one image; for every conv row of the band (2 BP + 1, the
 // first one is the halo shared with the band above):
 //   warps 1-4  load the two new input rows (all 3 channels) into a 16-row ring (column c at byte
 //              c + 4, four zero bytes either side; the next conv row's loads are issued before this
-//              row's im2col), build the im2col tile of the conv row (ceil(CW / 128) M-tiles x 6 K
-//              steps, 32B-swizzled, pixel u of a tile in row u / 2 or 64 + u / 2), double-buffered;
-//   warp 0     TMEM owner / MMA issuer: M128 N64 K32 MMAs into one of two TMEM accumulators;
+//              row's records are built), build the records of the new input rows (ceil(CW / 128)
+//              M-tiles of 128 pixels x 32 bytes each, 32B-swizzled, pixel u of a tile in row u / 2 or
+//              64 + u / 2) in a ring of 10 input rows;
+//   warp 0     TMEM owner / MMA issuer: per conv row and M-tile, 7 M128 N64 K32 MMAs (one per
+//              kernel row, A = that input row's records) into one of two TMEM accumulators;
 //   warps 5-12 (a lane quadrant x a 32-channel half each) requantise into a 3-row ring of conv
 //              outputs; after every odd conv row 2 py + 1 they max-pool pooled row py (conv rows
 //              2py-1 .. 2py+1) and write it out.
@@ -27,15 +33,16 @@ namespace dn8 {
 constexpr int ST_THREADS = 416;          // warp 0 MMA, 1-4 rows + im2col, 5-12 epilogue
 constexpr int ST_BP = 16;                 // pooled rows per band
 constexpr int ST_RING = 16;               // input row ring
-constexpr int ST_KSTEPS = 6;
-constexpr int ST_WBYTES = ST_KSTEPS * 64 * 32;   // prepared weights [6][64][32] swizzled
+constexpr int ST_KSTEPS = 7;
+constexpr int ST_WBYTES = ST_KSTEPS * 64 * 32;   // prepared weights [7][64][32] swizzled
+constexpr int ST_REC = 10;                // record ring: input rows y at slot y mod 10
 
 struct StemGeo {
     int N, H, W;                           // input
     int CH, CW, PH, PW;                    // conv / pooled output
     int mt;                                // M-tiles per conv row
     int row_bytes;                         // one ring row of one channel: W + 8
-    size_t ring_off, a_off, conv_off, bar_off, smem;
+    size_t ring_off, rec_off, conv_off, bar_off, smem;
 };
 
 static StemGeo stem_geo(int N, int H, int W) {
@@ -47,7 +54,7 @@ static StemGeo stem_geo(int N, int H, int W) {
     size_t off = ST_WBYTES;                                               // weights at 0
     g.ring_off = off; off += static_cast<size_t>(ST_RING) * 3 * g.row_bytes;
     off = (off + 1023) / 1024 * 1024;
-    g.a_off = off; off += static_cast<size_t>(2) * g.mt * ST_KSTEPS * 4096;   // 2 buffers
+    g.rec_off = off; off += static_cast<size_t>(ST_REC) * g.mt * 4096;        // record ring
     g.conv_off = off; off += static_cast<size_t>(3) * g.mt * 128 * 64;        // 3 conv rows
     g.bar_off = off; off += 256 + 1024;                                       // kc, barriers
     g.smem = off + 1024;
@@ -60,12 +67,12 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
     uint8_t* sRing = smem + geo.ring_off;
-    uint8_t* sA = smem + geo.a_off;
+    uint8_t* sRec = smem + geo.rec_off;
     uint8_t* sC = smem + geo.conv_off;
     float* sKC = reinterpret_cast<float*>(smem + geo.bar_off);               // [128] k, c
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + geo.bar_off + 512);
-    uint64_t* fullA = bars;          // [2] im2col tile ready (4 producer warps)
-    uint64_t* emptyA = bars + 2;     // [2] MMA done with the tile
+    uint64_t* fullA = bars;          // [2] the records of conv row i ready (4 producer warps)
+    uint64_t* emptyA = bars + 2;     // [2] MMA done with conv row i (by row parity)
     uint64_t* accf = bars + 4;       // [2]
     uint64_t* acce = bars + 6;       // [2] (4 epilogue warps)
     uint64_t* wfull = bars + 8;      // weights landed
@@ -136,22 +143,23 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             bulk_g2s(sW, a.w, ST_WBYTES, &wfull[0]);
             bool ok_run = mbar_wait(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
             const uint32_t idesc = idesc_u8s8(128, 64);
-            const uint32_t a0 = smem_u32(sA), w0 = smem_u32(sW);
+            const uint32_t a0 = smem_u32(sRec), w0 = smem_u32(sW);
             int i = 0;
             for (int t = 0; t < my_tasks && ok_run; ++t) {
                 int n, py0, cr0, nrows;
                 task_rows(t, n, py0, cr0, nrows);
                 for (int r = 0; r < nrows; ++r, ++i) {
-                    const int b = i & 1;
+                    const int b = i & 1, cr = cr0 + r;
                     if (!mbar_wait(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
                     if (!mbar_wait(&fullA[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
                     tc_fence_after();
                     for (int m = 0; m < MT; ++m)
 #pragma unroll
-                        for (int kk = 0; kk < ST_KSTEPS; ++kk) {
-                            const uint64_t ad = sdesc(a0 + ((b * MT + m) * ST_KSTEPS + kk) * 4096, 16, 256, LAYOUT_SW32);
-                            const uint64_t bd = sdesc(w0 + kk * 2048, 16, 256, LAYOUT_SW32);
-                            umma_u8s8(tmem + b * 128 + m * 64, ad, bd, idesc, kk ? 1u : 0u);   // first overwrites
+                        for (int ky = 0; ky < ST_KSTEPS; ++ky) {
+                            const int slot = ((2 * cr + ky - 3) % ST_REC + ST_REC) % ST_REC;   // input row's records
+                            const uint64_t ad = sdesc(a0 + (slot * MT + m) * 4096, 16, 256, LAYOUT_SW32);
+                            const uint64_t bd = sdesc(w0 + ky * 2048, 16, 256, LAYOUT_SW32);
+                            umma_u8s8(tmem + b * 128 + m * 64, ad, bd, idesc, ky ? 1u : 0u);   // first overwrites
                         }
                     umma_commit(&emptyA[b]);
                     umma_commit(&accf[b]);
@@ -236,44 +244,41 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                     fetch(n, 2 * cr + 5, pre1);
                 }
                 const int b = i & 1;
+                // the new records overwrite the slots last read by conv row i - 2 (and, at a band's
+                // first row, by conv row i - 1 too): wait until the MMAs of those rows are done
                 if (!mbar_wait(&emptyA[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
-                // im2col of the conv row: thread pt builds conv pixels u = 2p and 2p + 1 (p = pt % 64) of
-                // M-tile pt / 64, as tile rows p and p + 64 (the epilogue maps lane L back to pixel
-                // 2L or 2(L - 64) + 1), so a warp's 16-byte stores cover 32 consecutive rows; the two
-                // 8-byte windows start at ring bytes 2 cx and 2 cx + 2, so three aligned words per slot
-                // serve both
+                if (r == 0 && i > 0 &&
+                    !mbar_wait(&emptyA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
+                // records of the new input rows: thread pt builds conv pixels u = 2p and 2p + 1
+                // (p = pt % 64) of M-tile pt / 64, as tile rows p and p + 64 (the epilogue maps lane L
+                // back to pixel 2L or 2(L - 64) + 1); their 8-byte windows start at ring bytes 2 cx and
+                // 2 cx + 2, so three aligned words per channel serve both
                 if (pt < MT * 64) {
                     const int m = pt >> 6, r0 = pt & 63;
                     const int wb = 2 * min(m * 128 + 2 * r0, CW - 2);  // pixels past the conv width: junk rows
-                    uint8_t* tile = sA + (b * MT + m) * ST_KSTEPS * 4096;
-                    const int swz0 = ((r0 >> 2) & 1) << 4, swz1 = swz0;
+                    const int swz = ((r0 >> 2) & 1) << 4;
+                    const int y_first = r == 0 ? 2 * cr - 3 : 2 * cr + 2;
+                    const int y_end = 2 * cr + 4;
+                    for (int y = y_first; y < y_end; ++y) {
+                        uint32_t w0v[6], w1v[6];
 #pragma unroll
-                    for (int kk = 0; kk < ST_KSTEPS; ++kk) {
-                        uint32_t w0v[8], w1v[8];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int sl = kk * 4 + e;                // slot (ch, ky)
-                            if (sl < 21) {
-                                const int ch = sl / 7, ky = sl - ch * 7;
-                                const int y = 2 * cr + ky - 3;
-                                const uint8_t* row = sRing + ((y & (ST_RING - 1)) * 3 + ch) * RB + wb;
-                                const uint32_t u0 = *reinterpret_cast<const uint32_t*>(row);
-                                const uint32_t u1 = *reinterpret_cast<const uint32_t*>(row + 4);
-                                const uint32_t u2 = *reinterpret_cast<const uint32_t*>(row + 8);
-                                w0v[2 * e] = u0;
-                                w0v[2 * e + 1] = u1;
-                                w1v[2 * e] = __funnelshift_r(u0, u1, 16);
-                                w1v[2 * e + 1] = __funnelshift_r(u1, u2, 16);
-                            } else {
-                                w0v[2 * e] = w0v[2 * e + 1] = w1v[2 * e] = w1v[2 * e + 1] = 0u;
-                            }
+                        for (int ch = 0; ch < 3; ++ch) {
+                            const uint8_t* row = sRing + ((y & (ST_RING - 1)) * 3 + ch) * RB + wb;
+                            const uint32_t u0 = *reinterpret_cast<const uint32_t*>(row);
+                            const uint32_t u1 = *reinterpret_cast<const uint32_t*>(row + 4);
+                            const uint32_t u2 = *reinterpret_cast<const uint32_t*>(row + 8);
+                            w0v[2 * ch] = u0;
+                            w0v[2 * ch + 1] = u1;
+                            w1v[2 * ch] = __funnelshift_r(u0, u1, 16);
+                            w1v[2 * ch + 1] = __funnelshift_r(u1, u2, 16);
                         }
-                        uint8_t* d0 = tile + kk * 4096 + r0 * 32;
-                        *reinterpret_cast<uint4*>(d0 + swz0) = make_uint4(w0v[0], w0v[1], w0v[2], w0v[3]);
-                        *reinterpret_cast<uint4*>(d0 + (swz0 ^ 16)) = make_uint4(w0v[4], w0v[5], w0v[6], w0v[7]);
+                        const int slot = (y % ST_REC + ST_REC) % ST_REC;
+                        uint8_t* d0 = sRec + (slot * MT + m) * 4096 + r0 * 32;
+                        *reinterpret_cast<uint4*>(d0 + swz) = make_uint4(w0v[0], w0v[1], w0v[2], w0v[3]);
+                        *reinterpret_cast<uint4*>(d0 + (swz ^ 16)) = make_uint4(w0v[4], w0v[5], 0u, 0u);
                         uint8_t* d1 = d0 + 64 * 32;
-                        *reinterpret_cast<uint4*>(d1 + swz1) = make_uint4(w1v[0], w1v[1], w1v[2], w1v[3]);
-                        *reinterpret_cast<uint4*>(d1 + (swz1 ^ 16)) = make_uint4(w1v[4], w1v[5], w1v[6], w1v[7]);
+                        *reinterpret_cast<uint4*>(d1 + swz) = make_uint4(w1v[0], w1v[1], w1v[2], w1v[3]);
+                        *reinterpret_cast<uint4*>(d1 + (swz ^ 16)) = make_uint4(w1v[4], w1v[5], 0u, 0u);
                     }
                 }
                 fence_async_smem();

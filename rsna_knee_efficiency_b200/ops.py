@@ -85,9 +85,9 @@ def head_noalloc(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: in
 
 # --- weight preparation (numpy in, numpy out) ----------------------------------------------
 def prepare_stem_weights(w8: np.ndarray) -> np.ndarray:
-    """`S_w8` [64, 176] int8 -> the stem operand table (12288 bytes)."""
+    """`S_w8` [64, 176] int8 -> the stem operand table (14336 bytes)."""
     w8 = np.ascontiguousarray(w8, dtype=np.int8)
-    out = np.empty(12288, np.uint8)
+    out = np.empty(14336, np.uint8)
     nat.check(nat.lib().dn8_prepare_stem_weights(w8.ctypes.data, out.ctypes.data),
               "dn8_prepare_stem_weights")
     return out

@@ -122,11 +122,13 @@ def test_prepare_conv2_weights():
 def test_prepare_stem_weights():
     rng = np.random.default_rng(3)
     w8 = rng.integers(-127, 128, size=(64, 176), dtype=np.int64).astype(np.int8)
-    out = np.zeros(12288, np.uint8)
+    out = np.zeros(14336, np.uint8)
     assert _call(nat.lib().dn8_prepare_stem_weights, w8, out) == nat.DN8_OK
-    pad = np.zeros((64, 192), np.int8)
-    pad[:, :176] = w8
-    want = np.concatenate([_swz32(pad[:, k * 32:(k + 1) * 32]) for k in range(6)])
+    # one K step per kernel row ky: [ch 0 kx' 0..7 | ch 1 | ch 2 | 8 zeros] of S_w8's (ch, ky) slots
+    slots = w8[:, :168].reshape(64, 3, 7, 8)
+    steps = np.zeros((7, 64, 32), np.int8)
+    steps[:, :, :24] = slots.transpose(2, 0, 1, 3).reshape(7, 64, 24)
+    want = np.concatenate([_swz32(steps[ky]) for ky in range(7)])
     np.testing.assert_array_equal(out, want.view(np.uint8).reshape(-1))
 
 
