@@ -40,6 +40,9 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
             bv[k] = p.y;
             acc[k] = 0.0f;
         }
+        // (unrolled so that several pixels' loads are in flight; each channel's sum still runs in
+        // ascending pixel order)
+#pragma unroll 4
         for (int s = q; s < HW; s += 4) {
             const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + static_cast<size_t>(s) * 32));
             const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
