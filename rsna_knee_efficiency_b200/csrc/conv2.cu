@@ -117,29 +117,27 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = idesc_u8s8(128, 96);
-            const uint32_t x0 = smem_u32(sX), w0 = smem_u32(sW);
-            const bool wok = my_tiles == 0 || mbar_wait(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
-            for (int t = 0; t < my_tiles && wok; ++t) {
-                const int acc = t & 1, s = t % C2_STAGES;
-                if (!mbar_wait(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
-                tc_fence_after();
-                if (!mbar_wait(&full[s], (t / C2_STAGES) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
-                tc_fence_after();
-                const uint32_t xs = x0 + s * stage_bytes;
+        // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
+        const uint32_t idesc = idesc_u8s8(128, 96);
+        const uint32_t x0 = smem_u32(sX), w0 = smem_u32(sW);
+        const bool wok = my_tiles == 0 || mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+        for (int t = 0; t < my_tiles && wok; ++t) {
+            const int acc = t & 1, s = t % C2_STAGES;
+            if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            tc_fence_after();
+            if (!mbar_wait_w(&full[s], (t / C2_STAGES) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
+            tc_fence_after();
+            const uint32_t xs = x0 + s * stage_bytes;
 #pragma unroll
-                for (int dy = 0; dy < 3; ++dy)
+            for (int dy = 0; dy < 3; ++dy)
 #pragma unroll
-                    for (int cb = 0; cb < 4; ++cb) {
-                        const uint64_t ad = sdesc(xs + 2 * cb * PL + dy * W * 16, PL, 128, LAYOUT_NONE);
-                        const uint64_t bd = sdesc(w0 + (dy * 4 + cb) * 3072, 1536, 128, LAYOUT_NONE);
-                        umma_u8s8(tmem + acc * 128, ad, bd, idesc, (dy | cb) ? 1u : 0u);
-                    }
-                umma_commit(&empty[s]);
-                umma_commit(&accf[acc]);
-            }
+                for (int cb = 0; cb < 4; ++cb) {
+                    const uint64_t ad = sdesc(xs + 2 * cb * PL + dy * W * 16, PL, 128, LAYOUT_NONE);
+                    const uint64_t bd = sdesc(w0 + (dy * 4 + cb) * 3072, 1536, 128, LAYOUT_NONE);
+                    umma_u8s8_w(tmem + acc * 128, ad, bd, idesc, (dy | cb) ? 1u : 0u);
+                }
+            umma_commit_w(&empty[s]);
+            umma_commit_w(&accf[acc]);
         }
         __syncwarp();
     } else {

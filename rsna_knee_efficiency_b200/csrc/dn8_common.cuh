@@ -150,6 +150,38 @@ DN8_DEV void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(smem_u32(bar)) : "memory");
 }
+
+// ---- warp-converged MMA issue -----------------------------------------------------------------
+// The MMA role runs as one whole, converged warp: its control flow and operands are warp-uniform and
+// elect.sync picks the issuing lane (the lowest active one, so MMAs and their commits come from the
+// same thread) inside each asm. A lane-0-only issuer (a divergent branch) measured ~116 SM clocks per
+// M128 x N x K32 kind::i8 MMA on B200 for every N <= 128; the converged warp issues one every ~79
+// clocks at N = 128 (the tensor rate is 64).
+DN8_DEV void umma_u8s8_w(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "elect.sync l|e, 0xffffffff;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+DN8_DEV void umma_u8s8_ts_w(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "elect.sync l|e, 0xffffffff;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+DN8_DEV void umma_commit_w(uint64_t* bar) {
+    asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 l;\n\t"
+                 "elect.sync l|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+// Every lane waits; the warp continues only if all of them saw the phase (a timeout or an abort seen
+// by any lane stops the whole warp, so the issuing loop stays converged).
+DN8_DEV bool mbar_wait_w(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, abort_flag, code)) != 0;
+}
 // tcgen05.ld writes its registers asynchronously: their values may be read only after
 // tcgen05.wait::ld. A wait with a "memory" clobber alone orders memory, not registers, so the compiler
 // could schedule arithmetic on the loaded registers above it. The waits below name the registers of

@@ -14,11 +14,11 @@
 //
 // Pipeline stage = 4 "units" of 128 rows x 32 bytes (16 KB of A, 4 MMAs M128 x NC x K32, one
 // commit): conv1 takes 4 consecutive K groups per stage, the transition the 4 pixels of each
-// square of one K group. Every tcgen05 issue from the single MMA thread costs ~100-200 cycles, so
-// issuing 4 MMAs per wait / commit is what keeps the tensor core fed. The store bytes of a stage
+// square of one K group. Each MMA issue costs ~80 cycles even from a converged warp, so issuing 4
+// MMAs per wait / commit is what keeps the tensor core fed. The store bytes of a stage
 // arrive by bulk async copies into a shared-memory ring (explicit bytes in flight, no L1 staging).
 // Persistent, one CTA per SM, 19 warps:
-//   warp 0       TMEM owner and MMA issuer (lane 0).
+//   warp 0       TMEM owner and MMA issuer (the whole warp; one elected lane issues).
 //   warp 1       store producer: bulk copies into the raw ring (one lane per K group of a stage).
 //   warp 2       weight producer (lane 0): UMMA-ready weight tiles, resident when they fit.
 //   warps 3-10   prologue: one warp per unit, raw ring -> BN/ReLU/u8 -> 32B-swizzled operands.
@@ -185,54 +185,52 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     griddep_wait();                                    // the previous layer's store / bottleneck
 
     if (warp == 0) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
-            bool ok_run = true;
-            if (a.b_resident && T > 0) ok_run = mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
-            int i = 0;
-            for (int t = 0; t < my_tiles && ok_run; ++t) {
-                const int acc = t & 1;
-                const int chunk = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) % a.nchunks;
-                const uint32_t idesc = idesc_u8s8(128, min(NC, a.cout - chunk * NC));   // chunk width
-                if (!mbar_wait(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+        // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
+        const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+        bool ok_run = true;
+        if (a.b_resident && T > 0) ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+        int i = 0;
+        for (int t = 0; t < my_tiles && ok_run; ++t) {
+            const int acc = t & 1;
+            const int chunk = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) % a.nchunks;
+            const uint32_t idesc = idesc_u8s8(128, min(NC, a.cout - chunk * NC));   // chunk width
+            if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            tc_fence_after();
+            for (int j = 0; j < NS; ++j, ++i) {
+                const int s = i % SA;
+                const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
+                if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                uint32_t bbase;
+                int sbi = 0;
+                if (a.b_resident) {
+                    bbase = b0 + j * KSTEP * btile;
+                } else {
+                    sbi = i % a.sb;
+                    if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                    bbase = b0 + sbi * bstage;
+                }
                 tc_fence_after();
-                for (int j = 0; j < NS; ++j, ++i) {
-                    const int s = i % SA;
-                    const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
-                    if (!mbar_wait(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
-                    uint32_t bbase;
-                    int sbi = 0;
-                    if (a.b_resident) {
-                        bbase = b0 + j * KSTEP * btile;
-                    } else {
-                        sbi = i % a.sb;
-                        if (!mbar_wait(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
-                        bbase = b0 + sbi * bstage;
-                    }
-                    tc_fence_after();
-                    const uint32_t abase = a0 + s * ASTAGE;
+                const uint32_t abase = a0 + s * ASTAGE;
 #pragma unroll
-                    for (int x = 0; x < UNITS; ++x) {
-                        // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
-                        if (TRANS || x < gc) {
-                            const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
-                            const uint32_t accum = (j | x) ? 1u : 0u;   // the tile's first MMA overwrites
-                            if constexpr (TMEM_A) {
-                                umma_u8s8_ts(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
-                                             idesc, accum);
-                            } else {
-                                const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
-                                umma_u8s8(tmem + acc * NC, ad, bd, idesc, accum);
-                            }
+                for (int x = 0; x < UNITS; ++x) {
+                    // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
+                    if (TRANS || x < gc) {
+                        const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
+                        const uint32_t accum = (j | x) ? 1u : 0u;   // the tile's first MMA overwrites
+                        if constexpr (TMEM_A) {
+                            umma_u8s8_ts_w(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
+                                           idesc, accum);
+                        } else {
+                            const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
+                            umma_u8s8_w(tmem + acc * NC, ad, bd, idesc, accum);
                         }
                     }
-                    umma_commit(&emptyA[s]);
-                    if (!a.b_resident) umma_commit(&emptyB[sbi]);
                 }
-                if (!ok_run) break;
-                umma_commit(&accf[acc]);
+                umma_commit_w(&emptyA[s]);
+                if (!a.b_resident) umma_commit_w(&emptyB[sbi]);
             }
+            if (!ok_run) break;
+            umma_commit_w(&accf[acc]);
         }
         __syncwarp();
     } else if (warp == 1) {

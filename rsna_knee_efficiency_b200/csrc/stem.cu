@@ -137,11 +137,14 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     };
 
     if (warp == 0) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0 && my_tasks > 0) {
-            mbar_expect_tx(&wfull[0], ST_WBYTES);
-            bulk_g2s(sW, a.w, ST_WBYTES, &wfull[0]);
-            bool ok_run = mbar_wait(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+        // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
+        if (my_tasks > 0) {
+            if (lane == 0) {
+                mbar_expect_tx(&wfull[0], ST_WBYTES);
+                bulk_g2s(sW, a.w, ST_WBYTES, &wfull[0]);
+            }
+            __syncwarp();
+            bool ok_run = mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
             const uint32_t idesc = idesc_u8s8(128, 64);
             const uint32_t a0 = smem_u32(sRec), w0 = smem_u32(sW);
             int i = 0;
@@ -150,8 +153,8 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 task_rows(t, n, py0, cr0, nrows);
                 for (int r = 0; r < nrows; ++r, ++i) {
                     const int b = i & 1, cr = cr0 + r;
-                    if (!mbar_wait(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
-                    if (!mbar_wait(&fullA[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                    if (!mbar_wait_w(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
+                    if (!mbar_wait_w(&fullA[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
                     tc_fence_after();
                     for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -159,10 +162,10 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                             const int slot = ((2 * cr + ky - 3) % ST_REC + ST_REC) % ST_REC;   // input row's records
                             const uint64_t ad = sdesc(a0 + (slot * MT + m) * 4096, 16, 256, LAYOUT_SW32);
                             const uint64_t bd = sdesc(w0 + ky * 2048, 16, 256, LAYOUT_SW32);
-                            umma_u8s8(tmem + b * 128 + m * 64, ad, bd, idesc, ky ? 1u : 0u);   // first overwrites
+                            umma_u8s8_w(tmem + b * 128 + m * 64, ad, bd, idesc, ky ? 1u : 0u);   // first overwrites
                         }
-                    umma_commit(&emptyA[b]);
-                    umma_commit(&accf[b]);
+                    umma_commit_w(&emptyA[b]);
+                    umma_commit_w(&accf[b]);
                 }
             }
         }
