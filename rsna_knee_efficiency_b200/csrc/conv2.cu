@@ -152,9 +152,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         const int yl = p / W, x = p - yl * W;
         const bool has_l = x > 0, has_r = x < W - 1;
         const bool at_l = lane == 0, at_r = lane == 31;
-        float sc[16];                                         // this channel half's output scales
-#pragma unroll
-        for (int o = 0; o < 16; ++o) sc[o] = sSc[ch * 16 + o];
+        const float4* sc4 = reinterpret_cast<const float4*>(sSc + ch * 16);   // this half's output scales
         const int ql = quad > 0 ? quad - 1 : 0, qr = quad < 3 ? quad + 1 : 3;
 
         auto load = [&](int t, uint32_t (&d0)[16], uint32_t (&d1)[16], uint32_t (&d2)[16]) -> bool {
@@ -192,9 +190,23 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         auto wait_x = [&](int t) -> bool {
             return mbar_wait(&xbar[(t % C2_XBUF) * 2 + ch], (t / C2_XBUF) & 1, a.err, s_abort, ERR_WAIT_ACC);
         };
-        // out[p] = D[p-1][0] + D[p][1] + D[p+1][2] (zero outside the row), requantised (exchange t done)
-        auto finish = [&](int t, const uint32_t (&d0)[16], const uint32_t (&d1)[16], const uint32_t (&d2)[16]) {
+        // out[p] = D[p-1][0] + D[p][1] + D[p+1][2] (zero outside the row). The in-warp neighbours are
+        // added right after the load (so 16 sums, not 48 taps, stay live across the exchange);
+        // lanes 0 and 31 add the other quads' edge taps once exchange t is done.
+        auto fold = [&](const uint32_t (&d0)[16], const uint32_t (&d1)[16], const uint32_t (&d2)[16],
+                        int32_t (&sum)[16]) {
+            const bool in_l = has_l && !at_l, in_r = has_r && !at_r;
+#pragma unroll
+            for (int o = 0; o < 16; ++o) {
+                const uint32_t l = __shfl_up_sync(0xffffffffu, d0[o], 1);
+                const uint32_t r = __shfl_down_sync(0xffffffffu, d2[o], 1);
+                sum[o] = static_cast<int32_t>(d1[o]) + (in_l ? static_cast<int32_t>(l) : 0) +
+                         (in_r ? static_cast<int32_t>(r) : 0);
+            }
+        };
+        auto finish = [&](int t, const int32_t (&sum)[16]) {
             const int32_t* xq = xb + ((t % C2_XBUF) * 2 + ch) * 4 * 32;
+            const bool ex_l = has_l && at_l, ex_r = has_r && at_r;
             uint32_t wd[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -202,19 +214,17 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
                 const uint4 er = *reinterpret_cast<const uint4*>(xq + qr * 32 + 16 + 4 * j);
                 const uint32_t le[4] = {el.x, el.y, el.z, el.w};
                 const uint32_t re[4] = {er.x, er.y, er.z, er.w};
+                const float4 s4 = sc4[j];                             // broadcast read, 4 scales
+                const float sc[4] = {s4.x, s4.y, s4.z, s4.w};
                 uint32_t q[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const int o = 4 * j + k;
-                    const uint32_t l = __shfl_up_sync(0xffffffffu, d0[o], 1);
-                    const uint32_t r = __shfl_down_sync(0xffffffffu, d2[o], 1);
-                    const int32_t lv = has_l ? static_cast<int32_t>(at_l ? le[k] : l) : 0;
-                    const int32_t rv = has_r ? static_cast<int32_t>(at_r ? re[k] : r) : 0;
-                    const int32_t accv = static_cast<int32_t>(d1[o]) + lv + rv;
+                    const int32_t accv = sum[4 * j + k] + (ex_l ? static_cast<int32_t>(le[k]) : 0) +
+                                         (ex_r ? static_cast<int32_t>(re[k]) : 0);
                     const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
                                              : __int2float_rn(accv);
                     // rint(clamp(f sc, +-127)) as the low byte of (clamped + 1.5 * 2^23)
-                    q[k] = __float_as_uint(fminf(fmaxf(f * sc[o], -127.0f), 127.0f) + 12582912.0f);
+                    q[k] = __float_as_uint(fminf(fmaxf(f * sc[k], -127.0f), 127.0f) + 12582912.0f);
                 }
                 wd[j] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
             }
@@ -226,11 +236,15 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             }
         };
         for (int t = grp; t < my_tiles; t += 2) {
-            uint32_t d0[16], d1[16], d2[16];
-            if (!load(t, d0, d1, d2)) break;
-            publish(t, d0, d2);
+            int32_t sum[16];
+            {
+                uint32_t d0[16], d1[16], d2[16];
+                if (!load(t, d0, d1, d2)) break;
+                publish(t, d0, d2);
+                fold(d0, d1, d2, sum);
+            }
             if (!wait_x(t)) break;
-            finish(t, d0, d1, d2);
+            finish(t, sum);
         }
     }
 
