@@ -228,6 +228,23 @@ DN8_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
                    "r"(r[29]), "r"(r[30]), "r"(r[31])
                  : "memory");
 }
+// 32 lanes x 32 columns as two 16x256b.x4 stores (lanes +0 and +16 of the warp's quadrant):
+// thread t's registers 4k .. 4k+3 are (row t/4, columns 8k + 2(t%4), 8k + 2(t%4) + 1) and the same
+// columns of row t/4 + 8; r[0..15] go to the first 16 lanes, r[16..31] to the next 16.
+DN8_DEV void tmem_st16x256_2x4(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], "
+                 "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+                   "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+                   "r"(r[15])
+                 : "memory");
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], "
+                 "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                 ::"r"(taddr + (16u << 16)), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+                   "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+                   "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+                 : "memory");
+}
 DN8_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // tcgen05.st reads its source registers asynchronously: they must keep their values until
 // tcgen05.wait::st. This wait names them as inputs, so the compiler keeps them live (and does not

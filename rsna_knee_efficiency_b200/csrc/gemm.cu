@@ -32,13 +32,14 @@ constexpr int GM_WARPS = 19;
 constexpr int GM_THREADS = 32 * GM_WARPS;
 constexpr int SMEM_BUDGET = 225 * 1024;
 
-// KSTEP K groups of KSUB sub-tiles per stage (KSTEP * KSUB = 4 units); SR raw slots, SA operand slots
+// KSTEP K groups of KSUB sub-tiles per stage (KSTEP * KSUB = 4 units); SR raw slots (the transition's;
+// conv1 sizes its ring at launch), SA operand slots
 template <bool TRANS> struct GemmCfg;
 // conv1 keeps its A operands in TMEM (columns 256..511 behind the two 128-column accumulators:
 // SA = 8 stages of 4 units x 8 columns); the transition (NC up to 256 accumulator columns) keeps
 // them in shared memory.
 template <> struct GemmCfg<false> {                // conv1
-    static constexpr int KSUB = 1, KSTEP = 4, SR = 4, SA = 8;
+    static constexpr int KSUB = 1, KSTEP = 4, SA = 8;
     static constexpr bool TMEM_A = true;
 };
 template <> struct GemmCfg<true> {                 // transition
@@ -62,6 +63,7 @@ struct GemmArgs {
     int b_resident;           // 1: all G weight tiles stay in shared memory
     int sb;                   // weight ring stages when streamed
     int raw_bytes;            // raw ring slot size (a whole stage)
+    int sr;                   // raw ring slots
 };
 
 // Byte range [first, end) of the flattened input pixels (n * HW + y * W + x) a transition tile of
@@ -75,30 +77,46 @@ DN8_DEV void trans_span(int m0, int cnt, int HW, int W, int* first, int* end) {
     *end = n1 * HW + (2 * oy1 + 2) * W;
 }
 
-static size_t gemm_layout(bool trans, int G, int nc, int nchunks, int raw_bytes, int* sb, int* resident) {
-    const int sr = trans ? GemmCfg<true>::SR : GemmCfg<false>::SR, sa = trans ? GemmCfg<true>::SA : GemmCfg<false>::SA;
+// conv1's raw ring takes what shared memory is left after the weights (at least CONV1_SR_MIN and at
+// most CONV1_SR_MAX stages of 16 KB): with many K groups per tile a stage is held ~1,500 cycles by
+// the prologue, and four slots (64 KB in flight per SM) cap the store stream near 3 TB/s.
+constexpr int CONV1_SR_MIN = 4, CONV1_SR_MAX = 12;
+
+static size_t gemm_layout(bool trans, int G, int nc, int nchunks, int raw_bytes, int* sb, int* resident, int* sr_out) {
+    const int sr = trans ? GemmCfg<true>::SR : CONV1_SR_MIN, sa = trans ? GemmCfg<true>::SA : GemmCfg<false>::SA;
     const int kstep = trans ? GemmCfg<true>::KSTEP : GemmCfg<false>::KSTEP;
     const size_t a_smem = trans ? static_cast<size_t>(sa) * UNITS * 4096 : 0;     // conv1: A in TMEM
     const size_t fixed = static_cast<size_t>(sr) * raw_bytes + a_smem;
     const size_t misc = 1024 + static_cast<size_t>(G) * 256 + static_cast<size_t>(trans ? 640 : 128) * 8 + 8 * 96 + 64;
     const size_t btile = static_cast<size_t>(nc) * 32;
+    size_t used;
     if (nchunks == 1 && fixed + misc + btile * G <= SMEM_BUDGET) {
         *resident = 1;
         *sb = G;
-        return fixed + misc + btile * G;
+        used = fixed + misc + btile * G;
+    } else {
+        *resident = 0;
+        // streamed: a ring of `s` stages of kstep weight tiles
+        int s = static_cast<int>((SMEM_BUDGET - fixed - misc) / (btile * kstep));
+        s = s > 4 ? 4 : s;
+        *sb = s;
+        used = fixed + misc + btile * kstep * s;
     }
-    *resident = 0;
-    // streamed: a ring of `s` stages of kstep weight tiles
-    int s = static_cast<int>((SMEM_BUDGET - fixed - misc) / (btile * kstep));
-    s = s > 4 ? 4 : s;
-    *sb = s;
-    return fixed + misc + btile * kstep * s;
+    *sr_out = sr;
+    if (!trans && used <= SMEM_BUDGET) {
+        int extra = static_cast<int>((SMEM_BUDGET - used) / raw_bytes);
+        extra = extra > CONV1_SR_MAX - sr ? CONV1_SR_MAX - sr : extra;
+        *sr_out = sr + extra;
+        used += static_cast<size_t>(extra) * raw_bytes;
+    }
+    return used;
 }
 
 template <bool F16, bool TRANS>
 __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     using Cfg = GemmCfg<TRANS>;
-    constexpr int KSUB = Cfg::KSUB, KSTEP = Cfg::KSTEP, SR = Cfg::SR, SA = Cfg::SA;
+    constexpr int KSTEP = Cfg::KSTEP, SA = Cfg::SA;
+    const int SR = a.sr;
     constexpr int ASTAGE = UNITS * 4096;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -299,12 +317,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         __syncwarp();
     } else if (warp <= 10 && TMEM_A) {
         // ---------------- prologue, A into TMEM (conv1) ----------------
-        // Warp w writes TMEM lanes 32 (w % 4) .. + 31, so the four warps of one lane quadrant each
-        // take a quarter of the stage's rows: row r = 32 q + lane, all 4 units (K groups) of the
-        // stage; the two warps of a quadrant alternate stages.
+        // Warp w writes TMEM lanes 32 (w % 4) .. + 31; the two warps of a lane quadrant alternate
+        // stages. The stores use the 16x256b shape: thread t holds K bytes 8 (t % 4) .. + 7 (channels
+        // 8 (t % 4) .. + 7 of each unit's K group) of rows t / 4 + {0, 8, 16, 24} of the quadrant, so
+        // it needs only those 8 channels' BN pairs (two 16-byte table reads per unit) and its raw
+        // reads are 8-byte rows without bank conflicts.
         const int q = warp & 3, kk = (warp - 3) >> 2;
-        const int r = q * 32 + lane;
+        const int t0 = lane & 3, t1 = lane >> 2;
         const uint32_t tlane = static_cast<uint32_t>(q * 32) << 16;
+        const int roff = (q * 32 + t1) * 32 + t0 * 8;     // this thread's first raw bytes in a unit
         int j = kk;                                   // stage index within the tile (i = t * NS + j)
         while (j >= NS) j -= NS;
         for (int i = kk; i < T; i += 2) {
@@ -316,53 +337,46 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
             if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
             tc_fence_after();
-            // the stage's units (K groups): 32 raw bytes each -> 8 prologue words; all 4 units (32
-            // TMEM columns) in one store, whose registers stay live until tcgen05.wait::st
+            // res[16 h + 4 x + e]: unit x (K group), rows t/4 + 16 h (e < 2) and t/4 + 16 h + 8 (e >= 2),
+            // K bytes 8 (t % 4) + 4 (e & 1) .. + 3; the registers stay live until tcgen05.wait::st
             uint32_t res[32];
 #pragma unroll
             for (int x = 0; x < UNITS; ++x) {
-                uint32_t* rx = res + 8 * x;
                 if (x >= gc) {                                // short last stage: columns never read
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) rx[k] = 0u;
+                    for (int e = 0; e < 4; ++e) res[4 * x + e] = res[16 + 4 * x + e] = 0u;
                     continue;
                 }
                 const int g = j_this * KSTEP + x;
-                // (2-way bank conflicts on these two reads cost less than swapping the halves)
-                const uint8_t* src = sR + s * RB + x * 4096 + r * 32;
-                const uint4 lo = *reinterpret_cast<const uint4*>(src);
-                const uint4 hi = *reinterpret_cast<const uint4*>(src + 16);
+                const uint8_t* src = sR + s * RB + x * 4096 + roff;
+                const uint2 r0 = *reinterpret_cast<const uint2*>(src);            // row t/4
+                const uint2 r1 = *reinterpret_cast<const uint2*>(src + 8 * 32);   // row t/4 + 8
+                const uint2 r2 = *reinterpret_cast<const uint2*>(src + 16 * 32);  // row t/4 + 16
+                const uint2 r3 = *reinterpret_cast<const uint2*>(src + 24 * 32);  // row t/4 + 24
                 if (F16) {
-                    const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128);   // 32 channels
-                    uint4 tt = tb[0];
-                    rx[0] = prologue_f16x4(lo.x, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[1];
-                    rx[1] = prologue_f16x4(lo.y, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[2];
-                    rx[2] = prologue_f16x4(lo.z, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[3];
-                    rx[3] = prologue_f16x4(lo.w, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[4];
-                    rx[4] = prologue_f16x4(hi.x, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[5];
-                    rx[5] = prologue_f16x4(hi.y, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[6];
-                    rx[6] = prologue_f16x4(hi.z, tt.x, tt.y, tt.z, tt.w);
-                    tt = tb[7];
-                    rx[7] = prologue_f16x4(hi.w, tt.x, tt.y, tt.z, tt.w);
+                    const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128) + 2 * t0;
+                    const uint4 ta = tb[0], tc = tb[1];          // channels 8 t0 .. + 3, + 4 .. + 7
+                    res[4 * x + 0] = prologue_f16x4(r0.x, ta.x, ta.y, ta.z, ta.w);
+                    res[4 * x + 1] = prologue_f16x4(r0.y, tc.x, tc.y, tc.z, tc.w);
+                    res[4 * x + 2] = prologue_f16x4(r1.x, ta.x, ta.y, ta.z, ta.w);
+                    res[4 * x + 3] = prologue_f16x4(r1.y, tc.x, tc.y, tc.z, tc.w);
+                    res[16 + 4 * x + 0] = prologue_f16x4(r2.x, ta.x, ta.y, ta.z, ta.w);
+                    res[16 + 4 * x + 1] = prologue_f16x4(r2.y, tc.x, tc.y, tc.z, tc.w);
+                    res[16 + 4 * x + 2] = prologue_f16x4(r3.x, ta.x, ta.y, ta.z, ta.w);
+                    res[16 + 4 * x + 3] = prologue_f16x4(r3.y, tc.x, tc.y, tc.z, tc.w);
                 } else {
-                    const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32;
-                    rx[0] = prologue_f32x4(lo.x, tb);
-                    rx[1] = prologue_f32x4(lo.y, tb + 4);
-                    rx[2] = prologue_f32x4(lo.z, tb + 8);
-                    rx[3] = prologue_f32x4(lo.w, tb + 12);
-                    rx[4] = prologue_f32x4(hi.x, tb + 16);
-                    rx[5] = prologue_f32x4(hi.y, tb + 20);
-                    rx[6] = prologue_f32x4(hi.z, tb + 24);
-                    rx[7] = prologue_f32x4(hi.w, tb + 28);
+                    const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32 + 8 * t0;
+                    res[4 * x + 0] = prologue_f32x4(r0.x, tb);
+                    res[4 * x + 1] = prologue_f32x4(r0.y, tb + 4);
+                    res[4 * x + 2] = prologue_f32x4(r1.x, tb);
+                    res[4 * x + 3] = prologue_f32x4(r1.y, tb + 4);
+                    res[16 + 4 * x + 0] = prologue_f32x4(r2.x, tb);
+                    res[16 + 4 * x + 1] = prologue_f32x4(r2.y, tb + 4);
+                    res[16 + 4 * x + 2] = prologue_f32x4(r3.x, tb);
+                    res[16 + 4 * x + 3] = prologue_f32x4(r3.y, tb + 4);
                 }
             }
-            tmem_st32(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8), res);
+            tmem_st16x256_2x4(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8), res);
             __syncwarp();
             if (lane == 0) mbar_arrive(&freeR[s]);
             tmem_wait_st(res);
@@ -539,7 +553,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 
 template <bool F16, bool TRANS>
 static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
-    const size_t smem = gemm_layout(TRANS, g.G, g.nc, g.nchunks, g.raw_bytes, &g.sb, &g.b_resident) + 1024;
+    const size_t smem = gemm_layout(TRANS, g.G, g.nc, g.nchunks, g.raw_bytes, &g.sb, &g.b_resident, &g.sr) + 1024;
     if (smem > 227 * 1024 || g.sb < 2) return cudaErrorInvalidConfiguration;
     const int ntiles = ((g.rows + 127) / 128) * g.nchunks;
     const int grid = ntiles < sms ? ntiles : sms;
