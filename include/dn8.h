@@ -57,6 +57,10 @@ typedef struct dn8_conv1_args {
     int32_t* err;       /* device error word (0 = none) or NULL */
     int32_t G0, G, N, HW;
     int32_t prologue_f16;
+    /* 0: in0 / seg are the reference's group-major planes [G0][N*HW][32] / [G-G0][N*HW][32].
+     * > 0: in0 is a tile-major block store [ceil(N*HW/128)][tile_groups][128][32] (128 consecutive
+     * pixels per tile, all of a tile's groups contiguous) holding groups 0 .. G-1; seg and G0 are unused. */
+    int32_t tile_groups;
 } dn8_conv1_args;
 int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream);
 

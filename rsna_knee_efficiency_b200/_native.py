@@ -14,7 +14,7 @@ P, I32 = ctypes.c_void_p, ctypes.c_int32
 
 class Conv1Args(ctypes.Structure):
     _fields_ = [("in0", P), ("seg", P), ("w", P), ("ab", P), ("gd", P), ("out", P), ("err", P),
-                ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("prologue_f16", I32)]
+                ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("prologue_f16", I32), ("tile_groups", I32)]
 
 
 class Conv2Args(ctypes.Structure):

@@ -65,11 +65,15 @@ int dn8_device_sms(int device) {
 
 int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream) {
     if (a == nullptr) return fail(DN8_EINVAL, "dn8_conv1: null arguments");
-    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1)
-        return fail(DN8_EINVAL, "dn8_conv1: bad geometry G0=%d G=%d N=%d HW=%d", a->G0, a->G, a->N, a->HW);
-    if (static_cast<long long>(a->N) * a->HW * 128 >= (1ll << 31))
+    const bool tiled = a->tile_groups != 0;
+    if (a->G < 1 || a->N < 1 || a->HW < 1 || (!tiled && (a->G0 < 1 || a->G0 > a->G)) ||
+        (tiled && a->tile_groups < a->G))
+        return fail(DN8_EINVAL, "dn8_conv1: bad geometry G0=%d G=%d N=%d HW=%d tile_groups=%d", a->G0, a->G, a->N,
+                    a->HW, a->tile_groups);
+    if (static_cast<long long>(a->N) * a->HW * 128 >= (1ll << 31) ||
+        (tiled && static_cast<long long>((a->N * a->HW + 127) / 128) * a->tile_groups * 4096 >= (1ll << 40)))
         return fail(DN8_EINVAL, "dn8_conv1: N*HW*128 exceeds 2^31");
-    if (!aligned16(a->in0) || !aligned16(a->seg) || !aligned16(a->w) || !aligned16(a->ab) ||
+    if (!aligned16(a->in0) || (!tiled && !aligned16(a->seg)) || !aligned16(a->w) || !aligned16(a->ab) ||
         !aligned16(a->out) || a->gd == nullptr)
         return fail(DN8_EINVAL, "dn8_conv1: pointers must be non-null and 16-byte aligned");
     int sms = 0;

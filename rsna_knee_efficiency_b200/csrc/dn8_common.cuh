@@ -177,6 +177,55 @@ DN8_DEV void umma_commit_w(uint64_t* bar) {
                  "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
                  ::"r"(smem_u32(bar)) : "memory");
 }
+// ---- CTA pairs (clusters of two; tcgen05 cta_group::2) -------------------------------------------
+// The even CTA of a pair issues M = 256 MMAs whose A rows 0-127 / 128-255 and B rows (output
+// channels) 0-63 / 64-127 live in CTA 0 / CTA 1 at the same TMEM / shared-memory offsets; each CTA's
+// TMEM receives its own 128 accumulator rows. A CTA signals the other one by arriving on the barrier
+// at the same offset in its shared memory; the data it hands over is in TMEM (ordered by the tcgen05
+// waits and fences around the arrive) or was written by the async proxy, so the arrive needs no
+// cluster-scope release (which would also wait for the thread's global stores).
+DN8_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of both CTAs (also a CTA-wide barrier).
+DN8_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrives on the barrier at the same shared-memory offset in CTA `rank` of the cluster.
+DN8_DEV void mbar_arrive_at(uint64_t* bar, uint32_t rank) {
+    asm volatile("{\n\t.reg .b32 ra;\n\t"
+                 "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+                 "mbarrier.arrive.shared::cluster.b64 _, [ra];\n\t}"
+                 ::"r"(smem_u32(bar)), "r"(rank) : "memory");
+}
+// One full warp of EACH CTA of the pair (the same warp) allocates; both get the same base address.
+DN8_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+DN8_DEV void tmem_free_pair(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
+}
+// D (+)= A[tmem] * B[smem]^T over both CTAs of the pair (M = 256), issued from the even CTA by a
+// converged warp (one elected lane).
+DN8_DEV void umma_u8s8_ts_pair_w(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                 uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "elect.sync l|e, 0xffffffff;\n\t"
+                 "@e tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u) : "memory");
+}
+// Arrives once on `bar` in BOTH CTAs of the pair when the pair MMAs issued so far have completed.
+DN8_DEV void umma_commit_pair_w(uint64_t* bar) {
+    asm volatile("{\n\t.reg .pred e;\n\t.reg .b32 l;\n\t"
+                 "elect.sync l|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}"
+                 ::"r"(smem_u32(bar)), "h"(static_cast<uint16_t>(3)) : "memory");
+}
 // Every lane waits; the warp continues only if all of them saw the phase (a timeout or an abort seen
 // by any lane stops the whole warp, so the issuing loop stays converged).
 DN8_DEV bool mbar_wait_w(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code) {

@@ -64,6 +64,7 @@ struct GemmArgs {
     int sb;                   // weight ring stages when streamed
     int raw_bytes;            // raw ring slot size (a whole stage)
     int sr;                   // raw ring slots
+    int tg;                   // conv1: 0 = group-major planes; > 0 = tile-major store with tg groups per tile
 };
 
 // Byte range [first, end) of the flattened input pixels (n * HW + y * W + x) a transition tile of
@@ -88,7 +89,7 @@ static size_t gemm_layout(bool trans, int G, int nc, int nchunks, int raw_bytes,
     const size_t a_smem = trans ? static_cast<size_t>(sa) * UNITS * 4096 : 0;     // conv1: A in TMEM
     const size_t fixed = static_cast<size_t>(sr) * raw_bytes + a_smem;
     const size_t misc = 1024 + static_cast<size_t>(G) * 256 + static_cast<size_t>(trans ? 640 : 128) * 8 + 8 * 96 + 64;
-    const size_t btile = static_cast<size_t>(nc) * 32;
+    const size_t btile = static_cast<size_t>(trans ? nc : nc / 2) * 32;   // conv1: a CTA of the pair holds half
     size_t used;
     if (nchunks == 1 && fixed + misc + btile * G <= SMEM_BUDGET) {
         *resident = 1;
@@ -120,9 +121,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     constexpr int ASTAGE = UNITS * 4096;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // conv1 runs on CTA pairs: a tile is 256 rows, rows 128 r .. of it in CTA r, whose shared
+    // memory holds the weights of output channels 64 r .. + 63 (a 2 KB half of each K group's tile)
+    constexpr bool PAIR = !TRANS;
     const int NC = a.nc, G = a.G, G0 = a.G0, HW = a.HW, rows = a.rows;
-    const int btile = NC * 32, RB = a.raw_bytes;
+    const int btile = (PAIR ? NC / 2 : NC) * 32, RB = a.raw_bytes;   // this CTA's weight tile bytes
     constexpr bool TMEM_A = Cfg::TMEM_A;
+    constexpr int MT = PAIR ? 256 : 128;                         // rows per tile
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);   // pair / CTA
+    const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
     uint8_t* sR = smem;                                          // [SR][RB] raw store bytes
     uint8_t* sA = sR + SR * RB;                                  // [SA][KSUB][128][32] swizzled (transition)
     uint8_t* sB = sA + (TMEM_A ? 0 : SA * ASTAGE);               // weights
@@ -141,9 +149,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntm = (rows + 127) / 128;
+    const int ntm = (rows + MT - 1) / MT;
     const int ntiles = ntm * a.nchunks;
-    const int my_tiles = static_cast<int>(blockIdx.x) < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int my_tiles = unit < ntiles ? (ntiles - 1 - unit) / nunits + 1 : 0;
     const int NS = (G + KSTEP - 1) / KSTEP;                     // stages per tile
     const int T = my_tiles * NS;
     const uint32_t tcols = (NC > 128 || TMEM_A) ? 512u : 256u;
@@ -155,7 +163,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             mbar_init(&freeR[s], UNITS);
         }
         for (int s = 0; s < SA; ++s) {
-            mbar_init(&fullA[s], UNITS);
+            mbar_init(&fullA[s], PAIR ? 2 * UNITS : UNITS);        // pair: both CTAs' quadrant warps
             mbar_init(&emptyA[s], 1);
         }
         for (int s = 0; s < 8; ++s) {
@@ -164,7 +172,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         }
         for (int k = 0; k < 2; ++k) {
             mbar_init(&accf[k], 1);
-            mbar_init(&acce[k], 8);
+            mbar_init(&acce[k], PAIR ? 16 : 8);                     // pair: both CTAs' epilogue warps
         }
         *s_abort = 0;
         mbar_fence_init();
@@ -186,9 +194,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         if (TRANS) ok &= (p.x * 4194304.0f >= 127.0f) ? 1 : 0;
         else ok &= (fmaf(p.x, 4194304.0f, p.y) >= 1.0f && fmaf(p.x, -4194304.0f, p.y) <= 0.0f) ? 1 : 0;
     }
-    if (warp == 0) tmem_alloc(s_tmem, tcols);
+    if (warp == 0) {
+        if constexpr (PAIR) tmem_alloc_pair(s_tmem, tcols);
+        else tmem_alloc(s_tmem, tcols);
+    }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();               // also: both CTAs' barriers initialised
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
     tc_fence_before();
@@ -197,69 +209,90 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     if (warp == 2 && lane == 0 && T > 0 && a.b_resident) {
         // resident weights (constant: they may land while the previous kernel still runs)
         mbar_expect_tx(&fullB[0], static_cast<uint32_t>(G * btile));
-        bulk_g2s(sB, a.wu, static_cast<uint32_t>(G * btile), &fullB[0]);
+        if constexpr (PAIR) {
+            for (int g = 0; g < G; ++g)                       // this CTA's half of each K group's tile
+                bulk_g2s(sB + g * btile, a.wu + static_cast<size_t>(g) * 2 * btile + rank * btile,
+                         static_cast<uint32_t>(btile), &fullB[0]);
+        } else {
+            bulk_g2s(sB, a.wu, static_cast<uint32_t>(G * btile), &fullB[0]);
+        }
     }
     griddep_launch_dependents();
     griddep_wait();                                    // the previous layer's store / bottleneck
 
     if (warp == 0) {
-        // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
-        const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
-        bool ok_run = true;
-        if (a.b_resident && T > 0) ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
-        int i = 0;
-        for (int t = 0; t < my_tiles && ok_run; ++t) {
-            const int acc = t & 1;
-            const int chunk = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) % a.nchunks;
-            const uint32_t idesc = idesc_u8s8(128, min(NC, a.cout - chunk * NC));   // chunk width
-            if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
-            tc_fence_after();
-            for (int j = 0; j < NS; ++j, ++i) {
-                const int s = i % SA;
-                const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
-                if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
-                uint32_t bbase;
-                int sbi = 0;
-                if (a.b_resident) {
-                    bbase = b0 + j * KSTEP * btile;
-                } else {
-                    sbi = i % a.sb;
-                    if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
-                    bbase = b0 + sbi * bstage;
-                }
+        if (!PAIR || rank == 0) {
+            // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
+            // pair: the even CTA issues for both; its fullA / acce count both CTAs' warps, and every
+            // commit arrives in both CTAs
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+            bool ok_run = true;
+            if (a.b_resident && T > 0) {
+                ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+                if (PAIR && ok_run) ok_run = mbar_wait_w(&fullB[1], 0, a.err, s_abort, ERR_WAIT_FULL);   // the odd CTA's half
+            }
+            int i = 0;
+            for (int t = 0; t < my_tiles && ok_run; ++t) {
+                const int acc = t & 1;
+                const int chunk = (unit + t * nunits) % a.nchunks;
+                const uint32_t idesc = idesc_u8s8(MT, min(NC, a.cout - chunk * NC));   // chunk width
+                if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
                 tc_fence_after();
-                const uint32_t abase = a0 + s * ASTAGE;
+                for (int j = 0; j < NS; ++j, ++i) {
+                    const int s = i % SA;
+                    const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
+                    if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                    uint32_t bbase;
+                    int sbi = 0;
+                    if (a.b_resident) {
+                        bbase = b0 + j * KSTEP * btile;
+                    } else {
+                        sbi = i % a.sb;
+                        if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                        bbase = b0 + sbi * bstage;
+                    }
+                    tc_fence_after();
+                    const uint32_t abase = a0 + s * ASTAGE;
 #pragma unroll
-                for (int x = 0; x < UNITS; ++x) {
-                    // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
-                    if (TRANS || x < gc) {
-                        const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
-                        const uint32_t accum = (j | x) ? 1u : 0u;   // the tile's first MMA overwrites
-                        if constexpr (TMEM_A) {
-                            umma_u8s8_ts_w(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
-                                           idesc, accum);
-                        } else {
-                            const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
-                            umma_u8s8_w(tmem + acc * NC, ad, bd, idesc, accum);
+                    for (int x = 0; x < UNITS; ++x) {
+                        // conv1: unit x = K group j*KSTEP + x; transition: pixel x of the squares
+                        if (TRANS || x < gc) {
+                            const uint64_t bd = sdesc(bbase + (TRANS ? 0 : x * btile), 16, 256, LAYOUT_SW32);
+                            const uint32_t accum = (j | x) ? 1u : 0u;   // the tile's first MMA overwrites
+                            if constexpr (PAIR) {
+                                umma_u8s8_ts_pair_w(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
+                                                    idesc, accum);
+                            } else if constexpr (TMEM_A) {
+                                umma_u8s8_ts_w(tmem + acc * NC, tmem + TMEM_A_COL + s * (UNITS * 8) + x * 8, bd,
+                                               idesc, accum);
+                            } else {
+                                const uint64_t ad = sdesc(abase + x * 4096, 16, 256, LAYOUT_SW32);
+                                umma_u8s8_w(tmem + acc * NC, ad, bd, idesc, accum);
+                            }
                         }
                     }
+                    if constexpr (PAIR) {
+                        umma_commit_pair_w(&emptyA[s]);
+                    } else {
+                        umma_commit_w(&emptyA[s]);
+                        if (!a.b_resident) umma_commit_w(&emptyB[sbi]);
+                    }
                 }
-                umma_commit_w(&emptyA[s]);
-                if (!a.b_resident) umma_commit_w(&emptyB[sbi]);
+                if (!ok_run) break;
+                if constexpr (PAIR) umma_commit_pair_w(&accf[acc]);
+                else umma_commit_w(&accf[acc]);
             }
-            if (!ok_run) break;
-            umma_commit_w(&accf[acc]);
+            __syncwarp();
         }
-        __syncwarp();
     } else if (warp == 1) {
         // ---------------- store producer ----------------
         // Lane 0 waits for the slot and posts the stage's bytes; lanes 0 .. gc - 1 then each issue
         // one K group's copy (one instruction for the whole stage).
         int i = 0;
         for (int t = 0; t < my_tiles; ++t) {
-            const int tile = blockIdx.x + t * gridDim.x;
-            const int m0 = (tile / a.nchunks) * 128;
-            const int cnt = min(128, rows - m0);
+            const int tile = unit + t * nunits;
+            const int m0 = (tile / a.nchunks) * MT + static_cast<int>(rank) * 128;
+            const int cnt = min(128, rows - m0);               // pair: <= 0 past the last rows
             size_t off;
             uint32_t bytes;
             if (TRANS) {
@@ -267,9 +300,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 trans_span(m0, cnt, HW, a.W, &first, &end);
                 off = static_cast<size_t>(first) * 32;
                 bytes = static_cast<uint32_t>(end - first) * 32;
+            } else if (a.tg > 0) {
+                // tile-major: a stage is the tile's groups j*KSTEP .. in one contiguous run of 4 KB each
+                // (whole 128-row tiles are allocated, so a partial last tile is copied whole)
+                off = static_cast<size_t>(m0 >> 7) * a.tg * 4096;
+                bytes = cnt > 0 ? 4096u : 0u;
             } else {
-                off = static_cast<size_t>(m0) * 32;
-                bytes = static_cast<uint32_t>(cnt) * 32;
+                off = static_cast<size_t>(m0 < rows ? m0 : 0) * 32;
+                bytes = cnt > 0 ? static_cast<uint32_t>(cnt) * 32 : 0u;
             }
             bool ok_run = true;
             for (int j = 0; j < NS; ++j, ++i) {
@@ -281,7 +319,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     if (ok) mbar_expect_tx(&fullR[s], bytes * gc);
                 }
                 if (!__shfl_sync(0xffffffffu, ok, 0)) { ok_run = false; break; }
-                if (lane < gc) {                                     // one copy per K group, 4 KB apart
+                if (!TRANS && a.tg > 0) {
+                    if (lane == 0 && bytes > 0)
+                        bulk_g2s(sR + s * RB, a.in0 + off + static_cast<size_t>(j) * KSTEP * 4096,
+                                 static_cast<uint32_t>(gc) * 4096u, &fullR[s]);
+                } else if (lane < gc && bytes > 0) {                 // one copy per K group, 4 KB apart
                     const int g = j * KSTEP + lane;
                     const int8_t* src = g < G0 ? a.in0 + g * gstride + off : a.seg + (g - G0) * gstride + off;
                     bulk_g2s(sR + s * RB + lane * (RB / KSTEP), src, bytes, &fullR[s]);
@@ -293,10 +335,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     } else if (warp == 2) {
         // ---------------- weight producer ----------------
         if (lane == 0 && T > 0) {
+            if (PAIR && rank == 1 && a.b_resident) {
+                // this CTA's weight half has landed: tell the issuing CTA
+                if (mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL)) mbar_arrive_at(&fullB[1], 0);
+            }
             if (!a.b_resident) {
                 int i = 0;
                 for (int t = 0; t < my_tiles; ++t) {
-                    const int tile = blockIdx.x + t * gridDim.x;
+                    const int tile = unit + t * nunits;
                     const int chunk = tile % a.nchunks;
                     const int cbt = min(NC, a.cout - chunk * NC) * 32;      // weight tile bytes of the chunk
                     const uint8_t* wc = a.wu + static_cast<size_t>(G) * 32 * chunk * NC;
@@ -382,7 +428,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             tmem_wait_st(res);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fullA[sa]);
+            if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_at(&fullA[sa], 0);      // the issuing CTA's barrier
+                else mbar_arrive(&fullA[sa]);
+            }
         }
     } else if (warp <= 10) {
         // ---------------- prologue ----------------
@@ -404,7 +453,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 // pooled pixel m0 + r -> global pooled row gr (= n * H/2 + oy) and column ox; its input
                 // pixel (2 oy + dy, 2 ox + dx) sits 2W (gr - gr0) + dy W + 2 ox + dx pixels after the
                 // first pixel of the copied span
-                const int tile = blockIdx.x + t * gridDim.x;
+                const int tile = unit + t * nunits;
                 const int m0 = (tile / a.nchunks) * 128;
                 const int gr0 = m0 / W2;
                 int m = min(m0 + (lane >> 1), rows - 1);
@@ -477,11 +526,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int acc = t & 1;
             if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
             tc_fence_after();
-            const int tile = blockIdx.x + t * gridDim.x;
+            const int tile = unit + t * nunits;
             const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
             const int chunk = tile % nch;
             const int ncol = min(NC, a.cout - chunk * NC) >> 1;      // columns of this warp
-            const int m = (tile / nch) * 128 + quad * 32 + lane;
+            const int m = (tile / nch) * MT + static_cast<int>(rank) * 128 + quad * 32 + lane;
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
             // requantise 16 columns (output channels c0 ..) of this warp's 32 rows and store them
             auto finish = [&](const uint32_t (&v)[16], int cb) {
@@ -539,29 +588,81 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acce[acc]);
+            if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_at(&acce[acc], 0);      // the issuing CTA's barrier
+                else mbar_arrive(&acce[acc]);
+            }
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) {
+        // Every MMA has completed (the epilogue saw the last accumulator), but the issuing CTA's last
+        // commit arrivals on emptyA may still be landing here: wait for each barrier's final phase
+        // before the CTA can exit. Then both CTAs meet, so no arrival or MMA of the pair is in flight.
+        if (threadIdx.x == 0) {
+            for (int sl = 0; sl < SA && sl < T; ++sl) {
+                const int il = sl + SA * ((T - 1 - sl) / SA);          // last stage on barrier sl
+                if (!mbar_wait(&emptyA[sl], (il / SA) & 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+            }
+        }
+        cluster_sync();
+    }
     if (warp == 0) {
         tc_fence_after();
-        tmem_free(tmem, tcols);
+        if constexpr (PAIR) tmem_free_pair(tmem, tcols);
+        else tmem_free(tmem, tcols);
     }
+}
+
+// Clusters of two that can be resident at once (both SMs of a pair free), per device.
+static int pair_slots(int sms) {
+    static int cache[DN8_MAX_DEVICES] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= DN8_MAX_DEVICES) return sms / 2;
+    if (cache[dev] > 0) return cache[dev];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+    cfg.blockDim = dim3(GM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BUDGET + 1024;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaFuncSetAttribute(gemm_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BUDGET + 1024) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemm_kernel<true, false>, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = sms / 2;
+    }
+    n = n < sms / 2 ? n : sms / 2;
+    cache[dev] = n;
+    return n;
 }
 
 template <bool F16, bool TRANS>
 static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
     const size_t smem = gemm_layout(TRANS, g.G, g.nc, g.nchunks, g.raw_bytes, &g.sb, &g.b_resident, &g.sr) + 1024;
     if (smem > 227 * 1024 || g.sb < 2) return cudaErrorInvalidConfiguration;
-    const int ntiles = ((g.rows + 127) / 128) * g.nchunks;
-    const int grid = ntiles < sms ? ntiles : sms;
-    if (grid <= 0) return cudaSuccess;
+    if (!TRANS && !g.b_resident) return cudaErrorInvalidConfiguration;   // pairs keep the weights resident
+    const int mt = TRANS ? 128 : 256;
+    const int ntiles = ((g.rows + mt - 1) / mt) * g.nchunks;
+    if (ntiles <= 0) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, TRANS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    return launch_pdl(pdl, gemm_kernel<F16, TRANS>, dim3(grid), dim3(GM_THREADS), smem, st, g);
+    if (TRANS) {
+        const int grid = ntiles < sms ? ntiles : sms;
+        return launch_pdl(pdl, gemm_kernel<F16, TRANS>, dim3(grid), dim3(GM_THREADS), smem, st, g);
+    }
+    const int slots = pair_slots(sms);
+    const int pairs = ntiles < slots ? ntiles : slots;
+    return launch_pdl_pairs(pdl, gemm_kernel<F16, TRANS>, dim3(2 * pairs), dim3(GM_THREADS), smem, st, g);
 }
 
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool pdl) {
@@ -571,6 +672,7 @@ cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool
     g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.HW; g.W = 0;
     g.rows = a.N * a.HW; g.cout = 128; g.nc = 128; g.nchunks = 1;
     g.raw_bytes = 4 * 4096;
+    g.tg = a.tile_groups;
     return a.prologue_f16 ? launch_gemm<true, false>(g, sms, st, pdl) : launch_gemm<false, false>(g, sms, st, pdl);
 }
 

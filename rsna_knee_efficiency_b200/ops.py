@@ -21,11 +21,12 @@ def _stream(stream) -> int | None:
     return s.cuda_stream
 
 
-def conv1(in0: torch.Tensor, seg: torch.Tensor, w1: torch.Tensor, ab: torch.Tensor,
+def conv1(in0: torch.Tensor, seg: torch.Tensor | None, w1: torch.Tensor, ab: torch.Tensor,
           gd: torch.Tensor, out: torch.Tensor, G0: int, G: int, N: int, HW: int,
-          prologue_f16: bool, err: torch.Tensor | None = None, stream=None) -> None:
+          prologue_f16: bool, err: torch.Tensor | None = None, stream=None, tile_groups: int = 0) -> None:
+    """tile_groups = 0: in0 / seg are group-major planes; > 0: in0 is a tile-major block store."""
     a = nat.Conv1Args(_ptr(in0), _ptr(seg), _ptr(w1), _ptr(ab), _ptr(gd), _ptr(out), _ptr(err),
-                      G0, G, N, HW, int(bool(prologue_f16)))
+                      G0, G, N, HW, int(bool(prologue_f16)), int(tile_groups))
     nat.check(nat.lib().dn8_conv1(a, _stream(stream)), "dn8_conv1")
 
 

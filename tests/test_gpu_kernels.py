@@ -58,6 +58,32 @@ def test_conv1_ragged_rows(N, HW):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("bi,li,N,HW", [(0, 5, 2, 16384), (2, 20, 3, 1024), (3, 31, 2, 256), (1, 3, 3, 100),
+                                         (1, 3, 1, 7)])
+def test_conv1_tile_major_store(bi, li, N, HW):
+    """The tile-major block store ([tiles][tile_groups][128][32]) gives the oracle's bytes too,
+    including a partial last tile and a CTA pair whose second CTA has no rows."""
+    _, plan, par = plan_tables(512)
+    c0 = plan.blocks[bi].c0
+    cin = c0 + 32 * li
+    G, Gt = cin // 32, cin // 32 + 3
+    rows = N * HW
+    nt = (rows + 127) // 128
+    X = rand_store(np.random.default_rng(11 * bi + li), (N, HW, cin), "uniform").reshape(rows, cin)
+    tm = np.zeros((nt * 128, Gt, 32), dtype=np.int8)
+    tm[:rows, :G] = X.reshape(rows, G, 32)
+    tm = tm.reshape(nt, 128, Gt, 32).transpose(0, 2, 1, 3)
+    out = torch.full((8 * rows * 16,), 0xA5, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.conv1(dev(tm), None, dev(ops.prepare_conv1_weights(par[f"L{bi}_{li}_w1"])), dev(par[f"L{bi}_{li}_abh"]),
+              dev(par[f"L{bi}_{li}_gdu"]), out, 0, G, N, HW, True, err=err, tile_groups=Gt)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    want = orc.conv1(X, par[f"L{bi}_{li}_w1"], ab=None, abh=par[f"L{bi}_{li}_abh"], gd=par[f"L{bi}_{li}_gdu"],
+                     mode=orc.KERNEL)
+    np.testing.assert_array_equal(planes_to_pixels(out, rows), want)
+
+
 def _conv2_case(par, bi, li, N, H, W, seed):
     rng = np.random.default_rng(seed)
     V = rng.integers(0, 80, size=(N, H, W, 128), dtype=np.int64).astype(np.uint8)
