@@ -84,6 +84,15 @@ def test_conv1_tile_major_store(bi, li, N, HW):
     np.testing.assert_array_equal(planes_to_pixels(out, rows), want)
 
 
+@pytest.mark.parametrize("N,HW", [(1, 7), (3, 100), (2, 256)])
+def test_conv1_pairs_ragged_rows(N, HW):
+    """A layer whose weights only fit half per CTA (block 4, layer 32: 51 K groups) runs on CTA
+    pairs: 256-row tiles, including a pair whose second CTA has no rows."""
+    _, plan, par = plan_tables(512)
+    got, want = _conv1_case(par, 3, 31, plan.blocks[3].c0, N, HW, True, "relu", 5 * N + HW)
+    np.testing.assert_array_equal(got, want)
+
+
 def _conv2_case(par, bi, li, N, H, W, seed):
     rng = np.random.default_rng(seed)
     V = rng.integers(0, 80, size=(N, H, W, 128), dtype=np.int64).astype(np.uint8)
