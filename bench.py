@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--flip-tta", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--kernel", default=None, metavar="KIND:BLOCK:LAYER:N",
+                   help="profiling aid: 3 + 1 launches of one kernel (conv1 or conv2 of layer LAYER of "
+                        "block BLOCK, 0-based, on N images of random activations), then exit")
     return p.parse_args()
 
 
@@ -253,8 +256,51 @@ def roofline(enc, runner, hbm_gbs: float, i8_tops: float, peak_kind: str, vol_de
                         "roof_ms": round(roof_ms, 3), "int8_tops": i8_tops, "per_kind": summary}}
 
 
+def one_kernel(spec: str, img: int) -> None:
+    """Launches one dense-layer kernel 3 + 1 times on random activations, with the tables of a
+    seeded random DenseNet169 calibrated on synthetic batches (a small, fixed case for ncu)."""
+    import numpy as np
+    import torch
+    from rsna_knee_efficiency_b200 import densenet, ops, quant, synth
+    kind, bi, li, n = spec.split(":")
+    bi, li, n = int(bi), int(li), int(n)
+    torch.manual_seed(0)
+    m = densenet.random_init(densenet.DenseNet169(), 42)
+    cal = quant.calibrate(m, [torch.from_numpy(b) for b in synth.calibration_batches(2, 2, img, seed=1042)])
+    plan = quant.make_plan(m, cal, img)
+    par = quant.kernel_params(plan)
+    blk = plan.blocks[bi]
+    hw, rows = blk.h * blk.w, n * blk.h * blk.w
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    if kind == "conv1":
+        cin = blk.c0 + 32 * li
+        in0 = torch.randint(-127, 128, (rows * blk.c0,), dtype=torch.int8, device="cuda")
+        seg = torch.randint(-127, 128, (max(li, 1) * rows * 32,), dtype=torch.int8, device="cuda")
+        out = torch.empty(rows * 128, dtype=torch.uint8, device="cuda")
+        w1 = dev(ops.prepare_conv1_weights(par[f"L{bi}_{li}_w1"]))
+        ab, gd = dev(par[f"L{bi}_{li}_abh"]), dev(par[f"L{bi}_{li}_gdu"])
+        for _ in range(4):
+            ops.conv1(in0, seg, w1, ab, gd, out, blk.c0 // 32, cin // 32, n, hw, True, err=err)
+    elif kind == "conv2":
+        x = torch.randint(0, 80, (rows * 128,), dtype=torch.uint8, device="cuda")
+        out = torch.empty(rows * 32, dtype=torch.int8, device="cuda")
+        w2, sc = dev(ops.prepare_conv2_weights(par[f"L{bi}_{li}_w2k"])), dev(par[f"L{bi}_{li}_c2u"])
+        for _ in range(4):
+            ops.conv2(x, w2, sc, out, n, blk.h, blk.w, err=err)
+    else:
+        raise SystemExit(f"--kernel: unknown kind {kind!r} (conv1 or conv2)")
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise SystemExit(f"--kernel {spec}: device error {int(err.item())}")
+    print(f"--kernel {spec}: 4 launches, no device error")
+
+
 def main():
     args = parse()
+    if args.kernel:
+        one_kernel(args.kernel, args.img)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
