@@ -118,7 +118,7 @@ template <bool F16, bool TRANS, bool PAIR>
 __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     using Cfg = GemmCfg<TRANS>;
     constexpr int KSTEP = Cfg::KSTEP, SA = Cfg::SA;
-    const int SR = a.sr;
+    const int SR = TRANS ? GemmCfg<true>::SR : a.sr;            // transition: a fixed 4-stage ring
     constexpr int ASTAGE = UNITS * 4096;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
