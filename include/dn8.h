@@ -46,7 +46,9 @@ typedef void* dn8_stream; /* a cudaStream_t; NULL = legacy default stream */
  * Store: in0 [G0][N][HW][32] int8 (group-major: unlike the reference's [N][G0][HW][32], every
  * 32-channel group of a 128-pixel tile is one contiguous 4 KB run), seg [L][N][HW][32] int8
  * (groups G0.. read from seg).
- * Output: the u8 bottleneck as 8 planes of 16 channels, [8][N*HW][16]. */
+ * Output: the u8 bottleneck as 8 planes of 16 channels, [8][N*HW][16].
+ * G <= 70 (2240 input channels): the weights stay resident in shared memory, on single CTAs up to
+ * G = 37 and on clusters of two CTAs (half the weights each) above. */
 typedef struct dn8_conv1_args {
     const int8_t* in0;
     const int8_t* seg;

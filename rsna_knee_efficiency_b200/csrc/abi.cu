@@ -70,6 +70,8 @@ int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream) {
         (tiled && a->tile_groups < a->G))
         return fail(DN8_EINVAL, "dn8_conv1: bad geometry G0=%d G=%d N=%d HW=%d tile_groups=%d", a->G0, a->G, a->N,
                     a->HW, a->tile_groups);
+    if (!dn8::conv1_supported(a->G))
+        return fail(DN8_EINVAL, "dn8_conv1: G=%d K groups exceed the supported 70 (2240 input channels)", a->G);
     if (static_cast<long long>(a->N) * a->HW * 128 >= (1ll << 31) ||
         (tiled && static_cast<long long>((a->N * a->HW + 127) / 128) * a->tile_groups * 4096 >= (1ll << 40)))
         return fail(DN8_EINVAL, "dn8_conv1: N*HW*128 exceeds 2^31");

@@ -682,6 +682,13 @@ static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
     return cudaErrorInvalidConfiguration;
 }
 
+// conv1 keeps every layer's weights resident: on single CTAs up to 37 K groups, on CTA pairs up to 70.
+bool conv1_supported(int G) {
+    int sb = 0, resident = 0, sr = 0;
+    const size_t smem = gemm_layout(false, true, G, 128, 1, 4 * 4096, &sb, &resident, &sr) + 1024;
+    return resident && smem <= 227 * 1024;
+}
+
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool pdl) {
     GemmArgs g{};
     g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;

@@ -146,6 +146,12 @@ def test_kernel_entry_points_reject_bad_geometry_without_launching():
     assert lib.dn8_stem(ctypes.byref(s), None) == nat.DN8_EINVAL
     assert lib.dn8_conv1(None, None) == nat.DN8_EINVAL
     assert lib.dn8_last_error()
+    c = nat.Conv1Args()
+    c.G0, c.G, c.N, c.HW = 2, 71, 1, 64           # 71 K groups: the weights fit no launch shape
+    assert lib.dn8_conv1(ctypes.byref(c), None) == nat.DN8_EINVAL
+    assert b"exceed" in lib.dn8_last_error()
+    c.G, c.tile_groups = 8, 6                     # a tile-major store must hold all G groups
+    assert lib.dn8_conv1(ctypes.byref(c), None) == nat.DN8_EINVAL
 
 
 def test_zoom_rejects_bad_arguments_without_launching():
