@@ -132,25 +132,6 @@ constexpr uint32_t idesc_u8s8(int M, int N) {
     return (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
            (static_cast<uint32_t>(M >> 4) << 24);
 }
-// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
-DN8_DEV void umma_u8s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-                 ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem]^T: A (M = 128 rows, K = 32 bytes) in 8 consecutive TMEM columns,
-// row m in lane m, bytes 4c..4c+3 of the row in column c.
-DN8_DEV void umma_u8s8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
-                 ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// Arrives once on `bar` when every tcgen05 operation issued so far by this thread has completed.
-DN8_DEV void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(smem_u32(bar)) : "memory");
-}
-
 // ---- warp-converged MMA issue -----------------------------------------------------------------
 // The MMA role runs as one whole, converged warp: its control flow and operands are warp-uniform and
 // elect.sync picks the issuing lane (the lowest active one, so MMAs and their commits come from the
@@ -164,6 +145,8 @@ DN8_DEV void umma_u8s8_w(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32
                  "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
                  ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// A from TMEM: M = 128 rows x K = 32 bytes in 8 consecutive TMEM columns, row m in lane m, bytes
+// 4c .. 4c+3 of the row in column c.
 DN8_DEV void umma_u8s8_ts_w(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile("{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
                  "setp.ne.b32 p, %4, 0;\n\t"
@@ -265,17 +248,6 @@ DN8_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
                  "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                  : DN8_R8(0), DN8_R8(8)
                  : "r"(taddr) : "memory");
-}
-DN8_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-                 "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
-                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
-                   "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-                   "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
-                   "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-                   "r"(r[29]), "r"(r[30]), "r"(r[31])
-                 : "memory");
 }
 // 32 lanes x 32 columns as two 16x256b.x4 stores (lanes +0 and +16 of the warp's quadrant):
 // thread t's registers 4k .. 4k+3 are (row t/4, columns 8k + 2(t%4), 8k + 2(t%4) + 1) and the same
