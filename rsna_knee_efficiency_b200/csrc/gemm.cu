@@ -21,8 +21,14 @@
 //   warp 0       TMEM owner and MMA issuer (the whole warp; one elected lane issues).
 //   warp 1       store producer: bulk copies into the raw ring (one lane per K group of a stage).
 //   warp 2       weight producer (lane 0): UMMA-ready weight tiles, resident when they fit.
-//   warps 3-10   prologue: one warp per unit, raw ring -> BN/ReLU/u8 -> 32B-swizzled operands.
+//   warps 3-10   prologue: raw ring -> BN/ReLU/u8 -> the A operand (conv1: TMEM, two warps per
+//                lane quadrant taking alternate stages; transition: one warp per unit, 32B-swizzled
+//                shared memory).
 //   warps 11-18  epilogue: warp w reads TMEM lanes 32*(w%4).. and half of the NC columns.
+// conv1 layers whose weights do not fit one CTA run on CTA pairs (clusters of two, PAIR): 256-row
+// tiles, CTA r holding rows 128 r .. and the weights of output channels 64 r ..; the even CTA's
+// warp 0 issues M = 256 MMAs over both CTAs (tcgen05 cta_group::2), the odd CTA's prologue and
+// epilogue warps arrive on the even CTA's fullA / acce, and commits arrive in both CTAs.
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
