@@ -92,7 +92,7 @@ DN8_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
-// 4-D tiled tensor load (no multicast) into CTA shared memory, completing on `bar`.
+// 4-D tiled tensor load into this CTA's shared memory, completing on `bar`.
 DN8_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"

@@ -29,6 +29,8 @@
 // tiles, CTA r holding rows 128 r .. and the weights of output channels 64 r ..; the even CTA's
 // warp 0 issues M = 256 MMAs over both CTAs (tcgen05 cta_group::2), the odd CTA's prologue and
 // epilogue warps arrive on the even CTA's fullA / acce, and commits arrive in both CTAs.
+#include <atomic>
+
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
@@ -626,10 +628,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 
 // Clusters of two that can be resident at once (both SMs of a pair free), per device.
 static int pair_slots(int sms) {
-    static int cache[DN8_MAX_DEVICES] = {};
+    static std::atomic<int> cache[DN8_MAX_DEVICES];     // 0 = not looked up yet (threads may race to fill it)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= DN8_MAX_DEVICES) return sms / 2;
-    if (cache[dev] > 0) return cache[dev];
+    if (const int c = cache[dev].load(std::memory_order_relaxed); c > 0) return c;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
     cfg.blockDim = dim3(GM_THREADS);
@@ -649,7 +651,7 @@ static int pair_slots(int sms) {
         n = sms / 2;
     }
     n = n < sms / 2 ? n : sms / 2;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
