@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--flip-tta", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--lib", default=None, metavar="PATH",
+                   help="load this build of libdn8b200.so instead of the in-tree one (same-box A/B of two builds)")
     p.add_argument("--kernel", default=None, metavar="KIND:BLOCK:LAYER:N",
                    help="profiling aid: 3 + 1 launches of one kernel (conv1 or conv2 of layer LAYER of "
                         "block BLOCK, 0-based, on N images of random activations), then exit")
@@ -298,6 +300,10 @@ def one_kernel(spec: str, img: int) -> None:
 
 def main():
     args = parse()
+    if args.lib:
+        from rsna_knee_efficiency_b200 import _native
+        _native.LIB_PATH = Path(args.lib).resolve()
+        _native._lib = None
     if args.kernel:
         one_kernel(args.kernel, args.img)
         return
@@ -395,6 +401,7 @@ def main():
                        "img": args.img, "studies_per_gpu_step": S, "images_per_gpu_step": imgs_per_step,
                        "pass_images": runner.encoders[0].nb, "seeds": 2,
                        "parallelism": f"studies sharded over {world} GPU(s), no collective",
+                       "library": args.lib or "in-tree libdn8b200.so",
                        "l2": f"no flush: each step's working set (two block arenas, ~{runner.encoders[0].device_mb:.0f} "
                              f"MB per seed) far exceeds the 126 MB L2; the step's {S} studies repeat {pool} distinct synthetic studies"},
             "studies_per_s": round(value / (2 * runner.per_view), 3),
