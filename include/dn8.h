@@ -134,7 +134,7 @@ typedef struct dn8_head_args {
     const float* hw;        /* [n_out][C] float, or NULL (no head) */
     const float* hb;        /* [n_out] */
     float* logits;          /* [N][n_out] */
-    float* view_logits;     /* [N / per_view][n_out], or NULL */
+    float* view_logits;     /* [N / per_view][n_out], or NULL (needs hw: rejected without a head) */
     int32_t* tickets;       /* [N / per_view] zero-initialised device counters (left zeroed) */
     int32_t G0, G, N, HW, n_out, per_view;
     int32_t n_alloc;        /* images the store groups are laid out for (>= N; 0 = N) */

@@ -164,6 +164,8 @@ int dn8_head(const dn8_head_args* a, dn8_stream stream) {
         return fail(DN8_EINVAL, "dn8_head: bad pointers");
     if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
         return fail(DN8_EINVAL, "dn8_head: head without bias or logits buffer");
+    if (a->view_logits != nullptr && a->hw == nullptr)
+        return fail(DN8_EINVAL, "dn8_head: view_logits need the head (hw, hb, logits)");
     if (a->view_logits != nullptr && (a->per_view < 1 || a->N % a->per_view || a->tickets == nullptr))
         return fail(DN8_EINVAL, "dn8_head: views need per_view dividing N and a ticket array");
     cudaError_t e = dn8::launch_head(*a, static_cast<cudaStream_t>(stream));
@@ -196,6 +198,8 @@ int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
         return fail(DN8_EINVAL, "dn8_head_noalloc: bad pointers");
     if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
         return fail(DN8_EINVAL, "dn8_head_noalloc: head without bias or logits buffer");
+    if (a->view_logits != nullptr && a->hw == nullptr)
+        return fail(DN8_EINVAL, "dn8_head_noalloc: view_logits need the head (hw, hb, logits)");
     if (a->view_logits != nullptr && (a->per_view < 1 || a->N % a->per_view))
         return fail(DN8_EINVAL, "dn8_head_noalloc: views need per_view dividing N");
     dn8_head_args args = *a;

@@ -154,6 +154,31 @@ def test_kernel_entry_points_reject_bad_geometry_without_launching():
     assert lib.dn8_conv1(ctypes.byref(c), None) == nat.DN8_EINVAL
 
 
+def test_head_scratch_constant_matches_header(tmp_path):
+    """The Python binding's copy of DN8_HEAD_SCRATCH_VIEWS is the header's value."""
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "views.c"
+    src.write_text('#include <stdio.h>\n#include "dn8.h"\n'
+                   'int main(void) { printf("%d\\n", DN8_HEAD_SCRATCH_VIEWS); return 0; }\n')
+    exe = tmp_path / "views"
+    subprocess.run([gcc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    assert int(out) == nat.DN8_HEAD_SCRATCH_VIEWS
+
+
+@pytest.mark.parametrize("entry", ["dn8_head", "dn8_head_noalloc"])
+def test_head_rejects_view_logits_without_a_head(entry):
+    """view_logits with no head weights would never be written: refused before any CUDA call."""
+    lib = nat.lib()
+    fake = 1 << 20                                            # 16-byte aligned, never used
+    tickets = fake if entry == "dn8_head" else None
+    a = nat.HeadArgs(fake, fake, fake, None, None, None, None, fake, tickets, 20, 52, 6, 256, 0, 3, 0)
+    assert getattr(lib, entry)(ctypes.byref(a), None) == nat.DN8_EINVAL
+    assert b"need the head" in lib.dn8_last_error()
+
+
 def test_zoom_rejects_bad_arguments_without_launching():
     lib = nat.lib()
     fake = 1 << 20
