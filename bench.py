@@ -6,17 +6,22 @@
 
 Workload: synthetic studies of two crop windows (uint8 volumes of 26 x 512 x
 512 slices); two random-init DenseNet169 seeds (42, 43) calibrated at the 99.99th percentile over 8
-seeded batches; seed k reads window k (half-window budget); 24 slice triplets per window go
+seeded batches; each seed reads half of the study's 48 slice-triplet windows (the reference's
+`parx` design: seed f keeps position p of slot s where (p + s + f) % 2 == 0); the windows go
 through the fused stem (uint8 gather), 82 dense layers, 3 transitions and the pooling + linear head;
-study logits = mean over seeds of the slice-mean logits. A step = one call on `--studies` studies
-per GPU (2 x 24 x studies images). Studies are independent: ranks shard them with no collective on
-the data path (weak scaling); the logits are gathered on the host.
+study logits = mean over seeds of the per-seed window-mean logits. A step = one call on `--studies`
+studies per GPU (2 x 24 x studies images). Studies are independent: ranks shard them with no
+collective on the data path (weak scaling); the logits are gathered on the host.
 
 One JSON line (rank 0): `value` = images/s over all ranks with the study volumes resident in HBM;
 `e2e` = the same through the public API with the volumes copied from pinned host memory and the
 logits read back every step; `roofline` = the dominant kernel (conv1, all 82 layers) against the
-measured HBM copy bandwidth; `cpu_baseline` = the CPU port of the reference's INT8 path on this
-host. `--impl reference` times that CPU port alone (rank 0; other ranks exit).
+measured HBM copy bandwidth, with every kernel family in `roofline.network`; `sweep` = BASELINE
+config 4 (1, 4, 16, 64 studies per GPU per step); `layers` = BASELINE config 1 (one launch per
+layer shape on 24 images, summed per kernel and block); `cpu_baseline` = the CPU port of the
+reference's INT8 path on this host. `--impl reference` times that CPU port alone (rank 0; other
+ranks exit); `--layers [--impl reference]` prints the config-1 table of this repository's kernels
+(or of the reference's own sm_100 kernels) alone.
 """
 from __future__ import annotations
 
@@ -52,6 +57,14 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--lib", default=None, metavar="PATH",
                    help="load this build of libdn8b200.so instead of the in-tree one (same-box A/B of two builds)")
+    p.add_argument("--design", default="parx", help="window design of the two seeds (infer.member_windows)")
+    p.add_argument("--sweep", default="1,4,16,64",
+                   help="studies per GPU of the batch sweep (BASELINE config 4: 24, 96, 384, 1536 images per seed)")
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-layers", action="store_true", help="skip the config-1 micro-benchmark summary")
+    p.add_argument("--layers", action="store_true",
+                   help="only the config-1 micro-benchmark: one JSON line with every shape (ours, or with "
+                        "--impl reference the reference's own sm_100 kernels), then exit")
     p.add_argument("--kernel", default=None, metavar="KIND:BLOCK:LAYER:N",
                    help="profiling aid: 3 + 1 launches of one kernel (conv1 or conv2 of layer LAYER of "
                         "block BLOCK, 0-based, on N images of random activations), then exit")
@@ -183,6 +196,15 @@ def run_reference(args, rank: int):
 
 
 # ---- the GPU arm ------------------------------------------------------------------------------
+MAX_PASS = 768            # images per engine pass: conv1 addresses a block-1 launch below 2^31 bytes (< 1024 images)
+SWEEP_IMAGES = 24_000     # images per sweep point (steps = this / images per step, at least 3)
+
+
+def with_pass(pack: dict, n: int) -> dict:
+    """The same tables with `n` images per engine pass."""
+    return {**pack, "meta": {**pack["meta"], "n": int(n)}}
+
+
 def build_packs(img: int, dev: str, n: int):
     import torch
     from rsna_knee_efficiency_b200 import densenet, pack as packmod, quant, synth
@@ -216,13 +238,14 @@ def launch_work(kind: str, blk: dict, l: int, n: int, img: int) -> tuple[float, 
     return n * hw * ctot, 0
 
 
-def roofline(enc, runner, hbm_gbs: float, i8_tops: float, peak_kind: str, vol_dev):
-    """From the engine's per-launch CUDA events (one pass, averaged over 3): the dominant kernel
-    (conv1, all 82 layers: achieved = its algorithmic bytes / its time, against the measured HBM
-    copy bandwidth) and, per kernel family / block and for the whole pass, the fraction
+def roofline(runner, hbm_gbs: float, i8_tops: float, peak_kind: str, vol_dev):
+    """From the engine's per-launch CUDA events (one pass of the first seed, averaged over 3): the
+    dominant kernel (conv1, all 82 layers: achieved = its algorithmic bytes / its time, against the
+    measured HBM copy bandwidth) and, per kernel family / block and for the whole pass, the fraction
     t_roof / t_measured with t_roof = max(bytes / HBM, 2 MACs / INT8 peak) per launch."""
-    prof = enc.profile(planes=vol_dev[0].reshape(-1, vol_dev.shape[-2], vol_dev.shape[-1]), src=runner.src,
-                       flags=runner.flags, reps=3)
+    enc = runner.encoders[0]
+    prof = enc.profile(planes=vol_dev.reshape(-1, vol_dev.shape[-2], vol_dev.shape[-1]), src=runner.src[0],
+                       flags=runner.flags[0], reps=3)
     blocks = enc.meta["blocks"]
     n, img = enc.nb, enc.in_shape[2]
     per = {}
@@ -256,6 +279,247 @@ def roofline(enc, runner, hbm_gbs: float, i8_tops: float, peak_kind: str, vol_de
             "algorithmic_bytes_per_pass": int(c1[0]),
             "network": {"frac": round(roof_ms / pass_ms, 4), "pass_ms": round(pass_ms, 3),
                         "roof_ms": round(roof_ms, 3), "int8_tops": i8_tops, "per_kind": summary}}
+
+
+# ---- the single-layer micro-benchmark ----------------------------------------
+LAYER_IMAGES = 24
+# (side, block input channels c0, conv1 input channels swept) of blocks 1-4 at 512 px
+LAYER_BLOCKS = [(128, 64, range(64, 257, 32)), (64, 128, range(128, 513, 32)),
+                (32, 256, range(256, 1281, 32)), (16, 640, range(640, 1633, 32))]
+TRANS_SHAPES = [(128, 256), (64, 512), (32, 1280)]          # (side, c_tot) of transitions 1-3
+HEAD_SHAPE = (16, 640, 1664)                                # (side, c0, c_tot) of the last block
+FLUSH_BYTES = 512 << 20                                     # > the 126 MB L2, written before every launch
+
+
+class LayerData:
+    """Seeded config-1 inputs on the device: int8 stores drawn from the requantised ReLU
+    distribution (half zeros, the rest |N(0, 40)| clipped to 127), int8 weights ~U[-127, 127], BN
+    scale / shift ~N(1, 0.1) / N(0, 0.1) folded into the prologue tables (A = scale / 40, B = shift),
+    epilogue scales that spread the outputs over the u8 / int8 range."""
+
+    def __init__(self, seed: int = 1):
+        import torch
+        self.torch = torch
+        self.g = torch.Generator(device="cuda").manual_seed(seed)
+        self.rng = __import__("numpy").random.default_rng(seed)
+
+    def store(self, nbytes: int):
+        t = self.torch
+        v = t.randn(nbytes, generator=self.g, device="cuda").mul_(40).abs_().clamp_(max=127).round_()
+        v[t.rand(nbytes, generator=self.g, device="cuda") < 0.5] = 0
+        return v.to(t.int8)
+
+    def u8(self, nbytes: int):
+        return self.torch.randint(0, 256, (nbytes,), generator=self.g, device="cuda", dtype=self.torch.uint8)
+
+    def weights(self, shape):
+        return self.rng.integers(-127, 128, size=shape, dtype=__import__("numpy").int64).astype("int8")
+
+    def prologue(self, c: int):
+        """(ab [c, 2] float32, abh [c/2, 4] fp16 bits)."""
+        import numpy as np
+        from rsna_knee_efficiency_b200 import quant
+        ab = np.stack([self.rng.normal(1, 0.1, c) / 40.0, self.rng.normal(0, 0.1, c)], 1).astype(np.float32)
+        return ab, quant._abh(ab)
+
+    def epilogue(self, cout: int, k_in: int, u8_out: bool):
+        import numpy as np
+        g = self.rng.normal(1, 0.1, cout) / (4 * 128 * 73 * np.sqrt(k_in))
+        g = g * (1.0 if u8_out else 127.0)
+        return np.stack([g, np.zeros(cout)], 1).astype(np.float32)
+
+
+def _time_launch(fn, flush, reps: int = 7, warm: int = 2) -> float:
+    """Median device ms of `fn` (one launch on the current stream), each launch after an L2 flush
+    (a 512 MB write), bracketed by CUDA events on the launching stream. The flush also keeps the
+    GPU busy long enough for the host to enqueue the launch, so the events time the kernel alone."""
+    import torch
+    for _ in range(warm):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(reps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+
+def _roof_ms(nbytes: float, macs: float, hbm: float, i8: float) -> float:
+    return max(nbytes / (hbm * 1e9), 2 * macs / (i8 * 1e12)) * 1e3
+
+
+def layer_shapes():
+    """Every timed launch of config 1: (kind, block, c_in or c_tot, side, c0)."""
+    out = []
+    for bi, (side, c0, cins) in enumerate(LAYER_BLOCKS):
+        out += [("conv1", bi, cin, side, c0) for cin in cins]
+        out.append(("conv2", bi, 128, side, c0))
+    out += [("trans", bi, ctot, side, ctot) for bi, (side, ctot) in enumerate(TRANS_SHAPES)]
+    out.append(("head", 3, HEAD_SHAPE[2], HEAD_SHAPE[0], HEAD_SHAPE[1]))
+    return out
+
+
+def layer_work(kind: str, c: int, rows: int) -> tuple[float, float]:
+    """(algorithmic HBM bytes, MACs) of one config-1 launch over `rows` pixels (as `launch_work`)."""
+    if kind == "conv1":
+        return rows * (c + 128) + c * 128, rows * 128 * c
+    if kind == "conv2":
+        return rows * 160 + 36864, rows * 32 * 1152
+    if kind == "trans":
+        return rows * c + rows // 4 * c // 2 + c * c // 2, rows * c * c // 2
+    return rows * c, 0
+
+
+def layers_ours(hbm: float, i8: float, tile: bool = False) -> list:
+    """Config 1 through this repository's kernel entry points (include/dn8.h), one launch per
+    shape; `tile`: conv1 reads the tile-major block store."""
+    import numpy as np
+    import torch
+    from rsna_knee_efficiency_b200 import ops
+    d = LayerData()
+    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    flush = lambda: flush_buf.fill_(1)                                  # noqa: E731
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()    # noqa: E731
+    n, rows_out = LAYER_IMAGES, []
+    for kind, bi, c, side, c0 in layer_shapes():
+        hw = side * side
+        rows = n * hw
+        if kind == "conv1":
+            G = c // 32
+            out = torch.empty(rows * 128, dtype=torch.uint8, device="cuda")
+            w = dev(ops.prepare_conv1_weights(d.weights((G, 128, 32))))
+            abh_d = dev(d.prologue(c)[1])
+            gd = dev(d.epilogue(128, c, True))
+            if tile:
+                st = d.store(-(-rows // 128) * 128 * c)
+                fn = lambda: ops.conv1(st, None, w, abh_d, gd, out, 0, G, n, hw, True, err=err,  # noqa: E731
+                                       tile_groups=G)
+            else:
+                in0, seg = d.store(rows * c0), d.store(max(rows * (c - c0), 16))
+                fn = lambda: ops.conv1(in0, seg, w, abh_d, gd, out, c0 // 32, G, n, hw, True, err=err)  # noqa: E731
+        elif kind == "conv2":
+            x = d.u8(rows * 128)
+            out = torch.empty(rows * 32, dtype=torch.int8, device="cuda")
+            w2 = dev(ops.prepare_conv2_weights(d.weights((4, 9, 32, 32))))
+            sc = dev(d.epilogue(32, 1152, False)[:, 0].copy())
+            fn = lambda: ops.conv2(x, w2, sc, out, n, side, side, err=err)  # noqa: E731
+        elif kind == "trans":
+            G = c // 32
+            in0, seg = d.store(rows * c0 // 2), d.store(rows * c0 // 2)
+            out = torch.empty(rows // 4 * c // 2, dtype=torch.int8, device="cuda")
+            tw = dev(ops.prepare_trans_weights(d.weights((G, c // 2, 32))))
+            _, abh = d.prologue(c)
+            abh_d, gd = dev(abh), dev(d.epilogue(c // 2, c, False))
+            fn = lambda: ops.trans(in0, seg, tw, abh_d, gd, out, G // 2, G, n, side, side, True, err=err)  # noqa: E731
+        else:
+            in0, seg = d.store(rows * c0), d.store(rows * (c - c0))
+            fab = dev(d.prologue(c)[0])
+            feat = torch.empty((n, c), dtype=torch.float32, device="cuda")
+            fn = lambda: ops.head(in0, seg, fab, c0 // 32, c // 32, n, hw, feat=feat)  # noqa: E731
+        ms = _time_launch(fn, flush)
+        by, macs = layer_work(kind, c, rows)
+        roof = _roof_ms(by, macs, hbm, i8)
+        rows_out.append({"kind": kind, "block": bi, "c": c, "side": side, "rows": rows, "ms": round(ms, 4),
+                         "GBps": round(by / (ms * 1e-3) / 1e9, 1), "roof_ms": round(roof, 4),
+                         "frac": round(roof / ms, 3)})
+        del fn
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"config 1 micro-benchmark: device error {int(err.item())}")
+    return rows_out
+
+
+def layers_reference(hbm: float, i8: float) -> list:
+    """Config 1 through the reference's own sm_100 kernels (oracle/_ref, built from its source),
+    launched as the reference launches them: conv1_w64_pl, conv2_t8x32_pl (128 x 128) /
+    conv2_t16x16_pl, trans_w0 / trans_w1 (where c_out allows) and trans_q128, final_q."""
+    import numpy as np
+    import torch
+    from oracle import refcu
+    from rsna_knee_efficiency_b200 import quant
+    if not refcu.available():
+        raise RuntimeError("oracle/_ref not built (make -C oracle ref REF_DIR=<reference>/src/knee)")
+    rk = refcu.RefKernels(0)
+    d = LayerData()
+    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    flush = lambda: flush_buf.fill_(1)                                  # noqa: E731
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()    # noqa: E731
+    n, rows_out = LAYER_IMAGES, []
+    for kind, bi, c, side, c0 in layer_shapes():
+        hw = side * side
+        rows = n * hw
+        variants = []
+        if kind == "conv1":
+            G = c // 32
+            in0, seg = d.store(rows * c0), d.store(max(rows * (c - c0), 16))
+            out = torch.empty(rows * 128, dtype=torch.uint8, device="cuda")
+            w = dev(quant._chunked(d.weights((128, c)).astype(np.int8)))
+            abh = dev(d.prologue(c)[1])
+            gd = dev(d.epilogue(128, c, True))
+            variants.append(("conv1_w64_pl", lambda: rk.conv1(in0, seg, w, abh, gd, out, c0 // 32, G, n, hw, side)))
+        elif kind == "conv2":
+            x = d.u8(rows * 128)
+            out = torch.empty(rows * 32, dtype=torch.int8, device="cuda")
+            w2 = dev(d.weights((4, 9, 32, 32)))
+            sc = dev(d.epilogue(32, 1152, False)[:, 0].copy())
+            kern = "t8x32_pl" if side == 128 else "t16x16_pl"
+            variants.append((f"conv2_{kern}", lambda: rk.conv2(x, w2, sc, out, n, side, side, kern)))
+        elif kind == "trans":
+            G, cout = c // 32, c // 2
+            in0, seg = d.store(rows * c0 // 2), d.store(rows * c0 // 2)
+            out = torch.empty(rows // 4 * cout, dtype=torch.int8, device="cuda")
+            tw8 = d.weights((G, cout, 32))
+            ab, abh = d.prologue(c)
+            gdk = d.epilogue(cout, c, False)
+            twh, abh_d, abd = dev(tw8.astype(np.float16)), dev(abh), dev(ab)
+            gdf, gd = dev(gdk * 4), dev(gdk)
+            tw = dev(tw8)
+            for kind_w, bn in (("w0", 128), ("w1", 256)):
+                if cout % bn == 0:
+                    variants.append((f"trans_{kind_w}", lambda k=kind_w: rk.trans_w(k, in0, seg, twh, abh_d, gdf, out,
+                                                                                  G // 2, G, n, side, side)))
+            variants.append(("trans_q128", lambda: rk.trans_q128(in0, seg, tw, abd, gd, out, G // 2, G, n, side,
+                                                                 side)))
+        else:
+            in0, seg = d.store(rows * c0), d.store(rows * (c - c0))
+            fab = dev(d.prologue(c)[0])
+            feat = torch.empty((n, c), dtype=torch.float32, device="cuda")
+            variants.append(("final_q", lambda: rk.final_q(in0, c0 // 32, seg, n, hw, fab, feat, c)))
+        by, macs = layer_work(kind, c, rows)
+        roof = _roof_ms(by, macs, hbm, i8)
+        for name, fn in variants:
+            ms = _time_launch(fn, flush)
+            rows_out.append({"kind": kind, "kernel": name, "block": bi, "c": c, "side": side, "rows": rows,
+                             "ms": round(ms, 4), "GBps": round(by / (ms * 1e-3) / 1e9, 1),
+                             "roof_ms": round(roof, 4), "frac": round(roof / ms, 3)})
+        variants.clear()
+    torch.cuda.synchronize()
+    return rows_out
+
+
+def layers_summary(rows: list) -> dict:
+    """Per (kind, block): launches, ms, roof ms, fraction = sum roof / sum ms (each kind's fastest
+    kernel where a shape has several)."""
+    best = {}
+    for r in rows:
+        key = (r["kind"], r["block"], r["c"])
+        if key not in best or r["ms"] < best[key]["ms"]:
+            best[key] = r
+    agg = {}
+    for (kind, bi, _), r in best.items():
+        a = agg.setdefault(f"{kind}.b{bi}", [0, 0.0, 0.0])
+        a[0] += 1
+        a[1] += r["ms"]
+        a[2] += r["roof_ms"]
+    return {k: {"launches": v[0], "ms": round(v[1], 4), "roof_ms": round(v[2], 4), "frac": round(v[2] / v[1], 3)}
+            for k, v in agg.items()}
 
 
 def one_kernel(spec: str, img: int) -> None:
@@ -307,6 +571,20 @@ def main():
     if args.kernel:
         one_kernel(args.kernel, args.img)
         return
+    if args.layers:
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        import torch
+        torch.cuda.set_device(0)
+        hbm, i8, kind = peaks()
+        ref = args.impl == "reference"
+        rows = layers_reference(hbm, i8) if ref else layers_ours(hbm, i8)
+        print(json.dumps({"impl": "reference" if ref else "ours",
+                          "what": f"BASELINE config 1 micro-benchmark, {LAYER_IMAGES} images per shape, L2 flushed "
+                                  "before each launch, median of 7 launches (CUDA events on the launching stream)",
+                          "peak_hbm_gbs": hbm, "peak_int8_tops": i8, "peak_source": kind,
+                          "per_block": layers_summary(rows), "shapes": rows}), flush=True)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -322,99 +600,145 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device(dev))
-    # setup (untimed): packs, engines, the resident pool of synthetic studies
+    # setup (untimed): tables of both seeds (calibrated once), engines, the resident synthetic studies
     S = args.studies
-    per_view = 24 * (2 if args.flip_tta else 1)
-    packs = build_packs(args.img, dev, S * per_view)        # one pass per seed per step
-    pool = max(1, min(args.pool, S))
-    base = torch.from_numpy(make_volumes(pool, img=args.img, seed=10_000 * (rank + 1)))
-    vol_host = base[:, torch.arange(S) % pool].contiguous().pin_memory()      # [2, S, slices, H, W]
-    vol_dev = vol_host.to(dev)
-    runner = StudyRunner(packs, local, S, flip_tta=args.flip_tta)
-    blocks_per_pool = 1
-    imgs_per_step = runner.n_img * len(packs)
-
-    def step(i, src):
-        b = i % blocks_per_pool
-        return runner.run(src[:, b * S:(b + 1) * S])
+    plans = build_packs(args.img, dev, MAX_PASS)
+    sweep = [] if args.no_sweep else [int(v) for v in args.sweep.split(",") if v]
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for i in range(args.warmup):
-        step(i, vol_dev)
-    barrier()
-    for e in runner.encoders:
-        e.check()
-    # ---- value: inputs resident in HBM ----
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    with Clocks(local) as clk:
+    def max_over_ranks(*vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t]
+
+    def setup(studies):
+        per_seed = studies * 24 * (2 if args.flip_tta else 1)
+        runner = StudyRunner([with_pass(p, min(per_seed, MAX_PASS)) for p in plans], local, studies,
+                             flip_tta=args.flip_tta, design=args.design)
+        pool = max(1, min(args.pool, studies))
+        base = torch.from_numpy(make_volumes(pool, img=args.img, seed=10_000 * (rank + 1)))
+        vol_host = base[:, torch.arange(studies) % pool].contiguous().pin_memory()   # [2, S, slices, H, W]
+        return runner, vol_host, vol_host.to(dev), pool
+
+    def measure(runner, vol_host, vol_dev, studies, steps, warmup, clocks=None):
+        """(device ms of `steps` resident steps, device ms of the e2e loop over `steps` steps), each
+        the max over ranks, after `warmup` untimed steps."""
+        for _ in range(warmup):
+            runner.run(vol_dev)
+        barrier()
+        for e in runner.encoders:
+            e.check()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        if clocks is not None:
+            clocks.__enter__()
         ev0.record()
-        for i in range(args.steps):
-            step(i, vol_dev)
+        for _ in range(steps):
+            runner.run(vol_dev)
         ev1.record()
         barrier()
-    ms = ev0.elapsed_time(ev1)
-    # ---- e2e: the public study loop (`run_shard`) from pinned host volumes: every step copies its
-    # studies' volumes host -> device (overlapped with the previous step's encoders) and reads the
-    # study logits back into pinned host memory ----
-    steps_e2e = args.steps
-    order = torch.arange(steps_e2e * S) % S                      # every step's S studies, in order
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    logits_e2e = run_shard(runner, vol_host, studies=order)
-    e1.record()
-    barrier()
-    assert logits_e2e.shape == (steps_e2e * S, runner.n_out) and bool(torch.isfinite(logits_e2e).all())
-    ms_e2e = e0.elapsed_time(e1)
+        if clocks is not None:
+            clocks.__exit__(None, None, None)
+        ms = ev0.elapsed_time(ev1)
+        # e2e: the public study loop (`run_shard`) from pinned host volumes: every step copies its
+        # studies' volumes host -> device (overlapped with the previous step's encoders) and reads
+        # the study logits back into pinned host memory
+        order = torch.arange(steps * studies) % studies
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        logits = run_shard(runner, vol_host, studies=order)
+        e1.record()
+        barrier()
+        assert logits.shape == (steps * studies, runner.n_out) and bool(torch.isfinite(logits).all())
+        for e in runner.encoders:
+            e.check()
+        return max_over_ranks(ms, e0.elapsed_time(e1))
+
+    hbm, i8, peak_kind = peaks()
+    runner, vol_host, vol_dev, pool = setup(S)
+    imgs_per_step = runner.images_per_call
+    clk = Clocks(local)
+    ms, ms_e2e = measure(runner, vol_host, vol_dev, S, args.steps, args.warmup, clk)
+    value = imgs_per_step * args.steps * world / (ms * 1e-3)
+    e2e = imgs_per_step * args.steps * world / (ms_e2e * 1e-3)
+    imgs_per_study = imgs_per_step / S
+    roof = roofline(runner, hbm, i8, peak_kind, vol_dev) if rank == 0 else None
+    config_pass = runner.encoders[0].nb
+    device_mb = runner.encoders[0].device_mb
+    launches = runner.launches_per_call * args.steps
+    n_out = runner.n_out
+    h2d = int(vol_host[:, 0].numel() * S)
     for e in runner.encoders:
-        e.check()
-    # max over ranks (timing plumbing only)
-    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = float(t[0]), float(t[1])
-    total_imgs = imgs_per_step * args.steps * world
-    value = total_imgs / (ms * 1e-3)
-    e2e = imgs_per_step * steps_e2e * world / (ms_e2e * 1e-3)
-    clocks = clk.summary()
+        e.close()
+    del runner, vol_dev
+    torch.cuda.empty_cache()
+
+    # ---- BASELINE config 4: per-GPU batch sweep (images per seed pass per GPU) ----
+    sweep_out = []
+    for sv in sweep:
+        r2, vh, vd, _ = setup(sv)
+        steps = max(3, -(-SWEEP_IMAGES // (r2.images_per_call)))
+        m1, m2 = measure(r2, vh, vd, sv, steps, 3)
+        ips = r2.images_per_call * steps * world / (m1 * 1e-3)
+        row = {"studies_per_gpu": sv, "images_per_gpu_batch": r2.n_img[0], "pass_images": r2.encoders[0].nb,
+               "passes_per_seed": -(-r2.n_img[0] // r2.encoders[0].nb), "steps": steps,
+               "images_per_s": round(ips, 1), "studies_per_s": round(ips / (r2.images_per_call / sv), 2),
+               "e2e_images_per_s": round(r2.images_per_call * steps * world / (m2 * 1e-3), 1),
+               "ms_per_step": round(m1 / steps, 3)}
+        if rank == 0:
+            row["network_frac"] = roofline(r2, hbm, i8, peak_kind, vd)["network"]["frac"]
+        sweep_out.append(row)
+        for e in r2.encoders:
+            e.close()
+        del r2, vd
+        torch.cuda.empty_cache()
+        barrier()
+
+    # ---- BASELINE config 1: the single-layer micro-benchmark (rank 0, after the timed runs) ----
+    layers = None
+    if rank == 0 and not args.no_layers:
+        layers = layers_summary(layers_ours(hbm, i8))
+
     if rank == 0:
-        hbm, i8, kind = peaks()
-        roof = roofline(runner.encoders[0], runner, hbm, i8, kind, vol_dev)
         cpu = None
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(args.cpu_seconds, args.img)
             cpu["fp32_torch_images_per_s"] = fp32_cpu(args.img)
-        h2d = 2 * S * vol_host[0, 0].numel()
         print(json.dumps({
             "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "u8xs8->s32", "data": "synthetic",
-            "config": {"workload": f"two-seed study batch (BASELINE config 3 structure): {S} studies x 2 seeds x "
-                                   f"{runner.per_view} slice triplets per GPU per step, {args.img} px, uint8 "
-                                   f"volumes gathered by the stem{', flip TTA' if args.flip_tta else ''}",
+            "config": {"workload": f"two-seed study batch (BASELINE config 3 structure): {S} studies per GPU per "
+                                   f"step, 2 crop windows x 24 slice triplets per study, seed k reads the "
+                                   f"'{args.design}' half of the windows, {args.img} px, uint8 volumes gathered by "
+                                   f"the stem{', flip TTA' if args.flip_tta else ''}",
                        "img": args.img, "studies_per_gpu_step": S, "images_per_gpu_step": imgs_per_step,
-                       "pass_images": runner.encoders[0].nb, "seeds": 2,
+                       "pass_images": config_pass, "seeds": 2, "window_design": args.design,
                        "parallelism": f"studies sharded over {world} GPU(s), no collective",
                        "library": args.lib or "in-tree libdn8b200.so",
-                       "l2": f"no flush: each step's working set (two block arenas, ~{runner.encoders[0].device_mb:.0f} "
-                             f"MB per seed) far exceeds the 126 MB L2; the step's {S} studies repeat {pool} distinct synthetic studies"},
-            "studies_per_s": round(value / (2 * runner.per_view), 3),
+                       "l2": f"no flush: each step's working set (two block arenas, ~{device_mb:.0f} MB per seed) far "
+                             f"exceeds the 126 MB L2; the step's {S} studies repeat {pool} distinct synthetic studies"},
+            "studies_per_s": round(value / imgs_per_study, 3),
             "roofline": roof,
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e, 2), "unit": "images/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(S * runner.n_out * 4), "steps": steps_e2e,
+            "e2e": {"value": round(e2e, 2), "unit": "images/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": int(S * n_out * 4), "steps": args.steps,
                     "api": "infer.run_shard (pinned host volumes -> study logits in pinned host memory)"},
-            "gpu_launches": runner.launches_per_call * args.steps,
-            "clocks": clocks,
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "sweep": {"what": "BASELINE config 4: studies per GPU per step (24 images per seed pass per study; "
+                              f"passes of at most {MAX_PASS} images), at this world size", "points": sweep_out},
+            "layers": None if layers is None else
+            {"what": f"BASELINE config 1: one launch per shape on {LAYER_IMAGES} images, L2 flushed before each "
+                     "launch, summed per kernel and block (`--layers` prints every shape)", "per_block": layers},
         }), flush=True)
-    for e in runner.encoders:
-        e.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -4,8 +4,9 @@
 unmodified, by `make -C oracle ref` (nvcc -cubin -arch=sm_100 -std=c++14, the options of the
 reference's NVRTC build, src/knee/cudart.py:223-253). This module loads it through the CUDA driver
 API (into the current context, which torch owns) and launches single kernels with the reference's
-argument structs and launch geometry (src/knee/dense8s.py:1205-1290, :1330-1385). Only tests/ use
-it; the product never does.
+argument structs and launch geometry (src/knee/dense8s.py:1205-1290, :1330-1385). Only tests/ (as
+the byte checker) and bench.py's reference arm (`--impl reference --layers`, which times these
+kernels beside the BASELINE config 1 shapes) use it; the product never does.
 
 Layouts are the reference's: block input [N][G0][HW][32], layer segments [L][N][HW][32], planar u8
 bottleneck [4][N*HW][32], stem output = block 1's input [N][2][HW][32].
@@ -43,6 +44,11 @@ def gemm_shared(bm: int, mode: int, groups: int) -> int:
 def c2t_shared(th: int, tw: int) -> int:
     plane = -(-(th + 2) * (tw + 2) * 16 // 128) * 128 + 64
     return 36864 + 4 * plane + 128
+
+
+def trans_w_shared(bm: int, bn: int, groups: int) -> int:
+    """`trans_w_body<bm, bn>` (src/knee/dense8s.py:221-225)."""
+    return max(2 * (bm + bn) * 64, bm * (bn + 16)) + groups * 16 * 8
 
 
 STEM_I8_SMEM = -(-(64 * 176 + 512 + 5696 + 3 * 43 * 44) // 16) * 16 + 361 * 68
@@ -122,6 +128,20 @@ class RefKernels:
         a = KArg(in0.data_ptr(), seg.data_ptr(), tw.data_ptr(), ab.data_ptr(), gd.data_ptr(), out.data_ptr(),
                  G0, G, N, hw, W, rows, cout, cout // 32)
         self.launch("trans_q128", (cout // 128, -(-rows // 128)), (256,), [a], gemm_shared(128, 1, G))
+
+    def trans_w(self, kind, in0, seg, twh, abh, gdf, out, G0, G, N, H, W):
+        """The shipped wide transitions `trans_w0` / `trans_w1` (fp16 prologue, 2x2 mean before the
+        1x1 conv on fp16 tensor cores with fp32 accumulation; src/knee/dense8s_kernels.cu:3077-3268),
+        launched as `_trans_item` does (src/knee/dense8s.py:1242-1272): tables T*_wh, T*_abh, T*_gdf;
+        out = the next block's input in the reference layout [N][c_out/32][H*W/4][32]."""
+        bm, bn = {"w0": (256, 128), "w1": (128, 256)}[kind]
+        hw, cout = H * W, G * 16
+        if cout % bn:
+            raise ValueError(f"trans_{kind}: c_out {cout} not a multiple of {bn}")
+        rows = N * hw
+        a = KArg(in0.data_ptr(), seg.data_ptr(), twh.data_ptr(), abh.data_ptr(), gdf.data_ptr(), out.data_ptr(),
+                 G0, G, N, hw, W, rows, cout, cout // 32)
+        self.launch(f"trans_{kind}", (cout // bn, -(-(rows // 4) // bm)), (512,), [a], trans_w_shared(bm, bn, G))
 
     def stem_i8(self, x, w8, kc, out, N, H, W):
         if (H // 4) % STEM_TP or (W // 4) % STEM_TP or H != W:

@@ -16,6 +16,9 @@ stores:
     checked bit for bit without committing megabytes of weights;
   * `store_<b>`: the whole block store after block b, int8 [N, c_tot, h, w] (emulate's trace);
   * `feat`: the emulated features [N, 1664] float32.
+The 512-px case (the north star's resolution) keeps only `storehash_<b>` (sha256 of the store's
+bytes) and `xhash` instead of the stores and the input (which the test regenerates from the seeded
+synthetic volume), so the fixture stays a few kilobytes.
 """
 from __future__ import annotations
 
@@ -45,6 +48,16 @@ CASES = {
     "img64_flip": (64, 2, 42, 9, True, True),
     "img128_f16": (128, 2, 44, 10, True, False),
 }
+HASHED = {
+    # name: (img, images, model seed, volume seed, fp16 prologue everywhere, flip)
+    "img512_f16": (512, 2, 45, 11, True, False),
+}
+
+
+def input_images(img: int, n: int, vseed: int) -> np.ndarray:
+    """The case's uint8 images [n, 3, img, img]: n slice triplets spread over a seeded volume."""
+    t = synth.triplets(synth.volume(vseed, H=img, W=img))
+    return np.ascontiguousarray(t[np.linspace(0, len(t) - 1, n).round().astype(int)])
 
 
 def table_hash(a: np.ndarray) -> str:
@@ -55,7 +68,7 @@ def table_hash(a: np.ndarray) -> str:
 
 
 @torch.no_grad()
-def make(name: str, img: int, n: int, mseed: int, vseed: int, f16: bool, flip: bool) -> None:
+def make(name: str, img: int, n: int, mseed: int, vseed: int, f16: bool, flip: bool, hashed: bool = False) -> None:
     mine = densenet.random_init(densenet.DenseNet169(), mseed)
     ref = RefDenseNet()
     ref.load_state_dict(mine.state_dict())
@@ -64,8 +77,7 @@ def make(name: str, img: int, n: int, mseed: int, vseed: int, f16: bool, flip: b
     cal = dense8s.calibrate(ref, cal_x)
     plan = dense8s.make_plan(ref, cal, img)
     par = dense8s.kernel_params(plan)
-    t = synth.triplets(synth.volume(vseed, H=img, W=img))
-    x = np.ascontiguousarray(t[np.linspace(0, len(t) - 1, n).round().astype(int)])
+    x = input_images(img, n, vseed)
     xin = torch.from_numpy(x).double() / 255.0
     if flip:
         xin = torch.flip(xin, [-1])
@@ -84,12 +96,25 @@ def make(name: str, img: int, n: int, mseed: int, vseed: int, f16: bool, flip: b
         arrays[f"tab_{k}"] = np.frombuffer(table_hash(v).encode(), np.uint8)
     for bi, b in enumerate(plan.blocks):
         segs = [trace[(bi, j)] for j in range(len(b.layers) + 1)]
-        arrays[f"store_{bi}"] = torch.cat(segs, 1).round().to(torch.int8).numpy()
+        store = np.ascontiguousarray(torch.cat(segs, 1).round().to(torch.int8).numpy())
+        if hashed:
+            arrays[f"storehash_{bi}"] = np.frombuffer(table_hash(store).encode(), np.uint8)
+        else:
+            arrays[f"store_{bi}"] = store
+    if hashed:
+        arrays["xhash"] = np.frombuffer(table_hash(x).encode(), np.uint8)
+        arrays["xspec"] = np.frombuffer(json.dumps({"n": n, "vseed": vseed}).encode(), np.uint8)
+        del arrays["x"]
     np.savez_compressed(HERE / f"{name}.npz", **arrays)
     print(name, {k: v.shape for k, v in arrays.items() if k.startswith(("store", "feat", "x"))})
 
 
 if __name__ == "__main__":
     torch.manual_seed(0)
+    only = sys.argv[2:]                  # optional case names
     for name, args in CASES.items():
-        make(name, *args)
+        if not only or name in only:
+            make(name, *args)
+    for name, args in HASHED.items():
+        if not only or name in only:
+            make(name, *args, hashed=True)

@@ -123,3 +123,27 @@ def test_golden_emulate_tolerance(name):
     head = densenet.random_head(7)
     hw, hb = head.fc.weight.detach().numpy(), head.fc.bias.detach().numpy()
     assert np.abs((got @ hw.T + hb).mean(0) - (want @ hw.T + hb).mean(0)).max() < 5e-3
+
+
+def test_logits_512_within_1e3_of_reference_emulate_fixture():
+    """The north star's tolerance checked directly against the reference: the engine's logits at
+    512 px on the input of tests/golden/img512_f16.npz (tables from the reference's calibration)
+    within 1e-3 of the logits of the reference's own emulate() features (float64 head on the host),
+    and its features bit-exact to the oracle's KERNEL mode on the same input."""
+    from tests.golden_util import golden_case, golden_input, oracle_meta
+    z, meta, plan, par = golden_case("img512_f16")
+    x = golden_input("img512_f16")
+    n = len(x)
+    head = densenet.random_head(45)
+    enc = _encoder(plan, n, head)
+    vol = torch.from_numpy(np.ascontiguousarray(x.reshape(n * 3, 512, 512))).cuda()
+    src = torch.tensor([[3 * i, 3 * i + 1, 3 * i + 2, 0] for i in range(n)], dtype=torch.int32).cuda()
+    logits = torch.zeros((n, 4), dtype=torch.float32, device="cuda")
+    feats = enc.encode_u8(vol, src, logits=logits).cpu().numpy()
+    enc.check()
+    np.testing.assert_array_equal(feats, orc.forward(par, oracle_meta(plan, True), x, mode=orc.KERNEL))
+    hw, hb = head.fc.weight.detach().double().numpy(), head.fc.bias.detach().double().numpy()
+    want = z["feat"].astype(np.float64) @ hw.T + hb
+    err = float(np.abs(logits.cpu().numpy() - want).max())
+    print(f"512 px logits vs the reference's emulate(): max abs diff {err:.2e}")
+    assert err <= 1e-3

@@ -29,29 +29,30 @@ def _packs(n):
     return out
 
 
-@pytest.mark.parametrize("flip_tta", [False, True])
-def test_study_logits_match_oracle(flip_tta):
+@pytest.mark.parametrize("design,flip_tta", [("parx", False), ("parx", True), ("scale", False)])
+def test_study_logits_match_oracle(design, flip_tta):
+    """Seed k reads the windows `member_windows(design, 0, 2, 24, seed=k)` of both crop windows
+    ("parx": alternate positions of every slot; "scale": all of slot k)."""
     studies = 2
     per_view = (SLICES - 2) * (2 if flip_tta else 1)
     packs = _packs(studies * per_view)
-    runner = infer.StudyRunner([p for p, _, _ in packs], 0, studies, SLICES, flip_tta)
+    runner = infer.StudyRunner([p for p, _, _ in packs], 0, studies, SLICES, flip_tta, design=design)
     vols = infer.make_volumes(studies, img=IMG, slices=SLICES, seed=77)
     got = runner.run(torch.from_numpy(vols).cuda()).cpu().numpy()
     for e in runner.encoders:
         e.check()
+    planes = vols.reshape(-1, IMG, IMG)
     want = np.zeros((studies, 4))
     for k, (p, plan, head) in enumerate(packs):
         par = quant.kernel_params(plan)
         hw, hb = head.fc.weight.detach().double().numpy(), head.fc.bias.detach().double().numpy()
+        src, flags, _ = infer.plane_table(design, k, studies, SLICES, 2, flip_tta)
+        assert runner.per_view[k] == per_view
         for s in range(studies):
-            x = synth.triplets(vols[k % 2, s])
-            flips = np.zeros(len(x), np.int32)
-            if flip_tta:
-                x = np.concatenate([x, x])
-                flips = np.repeat(np.array([0, 1], np.int32), SLICES - 2)
-            f = orc.forward(par, packmod.pack_meta(plan, len(x)), x, flip=flips, mode=orc.KERNEL)
-            np.testing.assert_array_equal(
-                runner.encoders[k].out[s * per_view:(s + 1) * per_view].cpu().numpy(), f)
+            rows = slice(s * per_view, (s + 1) * per_view)
+            x = planes[src[rows, :3]]
+            f = orc.forward(par, packmod.pack_meta(plan, len(x)), x, flip=flags[rows], mode=orc.KERNEL)
+            np.testing.assert_array_equal(runner.encoders[k].out[rows].cpu().numpy(), f)
             want[s] += (f.astype(np.float64) @ hw.T + hb).mean(0) / len(packs)
     np.testing.assert_allclose(got, want, atol=1e-5)
 

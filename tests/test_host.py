@@ -198,3 +198,47 @@ def test_run_shard_with_study_indices():
     torch.testing.assert_close(infer.run_shard(_FakeRunner(3), vols, studies=order), want)
     a, b = infer.shard(len(order), 2, 1)
     torch.testing.assert_close(infer.run_shard(_FakeRunner(2), vols, rank=1, world=2, studies=order), want[a:b])
+
+
+def test_member_windows_match_the_reference():
+    """Every design, member and seed of tests/golden/member_windows.json (made by the reference's own
+    `member_windows`) at the benchmark's 2 x 24 and the submission's 8 x 11 geometry."""
+    import json
+    from pathlib import Path
+    cases = json.loads((Path(__file__).resolve().parent / "golden" / "member_windows.json").read_text())
+    assert len(cases) == 192
+    for c in cases:
+        got = infer.member_windows(c["design"], c["member"], c["n_slots"], c["per"], seed=c["seed"])
+        assert got.tolist() == c["windows"], c
+
+
+def test_parx_seeds_cover_every_window_once():
+    """Two seeds of `parx` read complementary halves: every (slot, position) exactly once, and each
+    seed alternate positions of every slot."""
+    per = 24
+    a = infer.member_windows("parx", 0, 2, per, seed=0)
+    b = infer.member_windows("parx", 0, 2, per, seed=1)
+    assert sorted(a.tolist() + b.tolist()) == list(range(2 * per))
+    for idx in (a, b):
+        for slot in range(2):
+            pos = idx[idx // per == slot] % per
+            assert len(pos) == per // 2 and set(np.diff(pos)) == {2}
+
+
+@pytest.mark.parametrize("flip", [False, True])
+def test_plane_table_addresses_the_seed_windows(flip):
+    """Image i of seed k reads the three slices of its window from the window-major volume planes."""
+    studies, slices = 3, 26
+    per = slices - 2
+    for seed in (0, 1):
+        src, flags, idx = infer.plane_table("parx", seed, studies, slices, 2, flip)
+        nf = 2 if flip else 1
+        assert src.shape == (studies * nf * len(idx), 4) and flags.shape == (len(src),)
+        i = 0
+        for st in range(studies):
+            for f in range(nf):
+                for w in idx:
+                    s, p = divmod(int(w), per)
+                    assert src[i, :3].tolist() == [(s * studies + st) * slices + p + d for d in range(3)]
+                    assert flags[i] == f
+                    i += 1

@@ -11,12 +11,12 @@ import torch
 
 from oracle import oracle as orc
 from rsna_knee_efficiency_b200 import densenet, quant, synth
-from tests.golden_util import CASES, golden_case, oracle_meta, table_hash
+from tests.golden_util import CASES, HASHED_CASES, golden_case, golden_input, oracle_meta, table_hash
 
-VSEED = {"img64_f16": 7, "img64_f32": 8, "img64_flip": 9, "img128_f16": 10}
+VSEED = {"img64_f16": 7, "img64_f32": 8, "img64_flip": 9, "img128_f16": 10, "img512_f16": 11}
 
 
-@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("name", CASES + HASHED_CASES)
 def test_tables_bit_identical_to_reference(name):
     z, meta, plan, par = golden_case(name)
     ref = {k[4:]: bytes(v).decode() for k, v in z.items() if k.startswith("tab_")}
@@ -25,7 +25,7 @@ def test_tables_bit_identical_to_reference(name):
     assert bad == []
 
 
-@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("name", CASES + HASHED_CASES)
 def test_calibration_matches_reference(name):
     z, meta, _, _ = golden_case(name)
     cal_ref = json.loads(bytes(z["cal"]).decode())
@@ -86,3 +86,16 @@ def test_oracle_stem_kernel_mode_matches_emulate_formula():
     want = z["store_0"][:, :64].transpose(0, 2, 3, 1)
     d = np.abs(q.astype(int) - want.astype(int))
     assert d.max() <= 2 and (d > 0).mean() < 1e-3
+
+
+@pytest.mark.parametrize("name", HASHED_CASES)
+def test_oracle_emulate_mode_bit_exact_512(name):
+    """At 512 px (the north star's resolution) EMULATE mode reproduces the reference's emulate():
+    the sha256 of every block store (emulate's trace) and the features."""
+    z, meta, plan, par = golden_case(name)
+    tr = {}
+    f = orc.forward(par, oracle_meta(plan, meta["f16"]), golden_input(name), flip=1 if meta["flip"] else None,
+                    mode=orc.EMULATE, trace=tr)
+    for bi, got in enumerate(_stores(tr, plan)):
+        assert table_hash(np.ascontiguousarray(got)) == bytes(z[f"storehash_{bi}"]).decode(), f"block {bi}"
+    np.testing.assert_allclose(f, z["feat"], rtol=1e-6, atol=1e-7)
