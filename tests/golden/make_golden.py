@@ -16,9 +16,9 @@ stores:
     checked bit for bit without committing megabytes of weights;
   * `store_<b>`: the whole block store after block b, int8 [N, c_tot, h, w] (emulate's trace);
   * `feat`: the emulated features [N, 1664] float32.
-The 512-px case (the north star's resolution) keeps only `storehash_<b>` (sha256 of the store's
-bytes) and `xhash` instead of the stores and the input (which the test regenerates from the seeded
-synthetic volume), so the fixture stays a few kilobytes.
+The 512-px case (the north star's resolution: one whole view, the 24 triplets of a volume) keeps
+only `storehash_<b>` (sha256 of each image's store bytes) and `xhash` instead of the stores and the
+input (which the test regenerates from the seeded synthetic volume), so the fixture stays small.
 """
 from __future__ import annotations
 
@@ -50,7 +50,7 @@ CASES = {
 }
 HASHED = {
     # name: (img, images, model seed, volume seed, fp16 prologue everywhere, flip)
-    "img512_f16": (512, 2, 45, 11, True, False),
+    "img512_f16": (512, 24, 45, 11, True, False),     # one whole view: the 24 triplets of a volume
 }
 
 
@@ -97,8 +97,9 @@ def make(name: str, img: int, n: int, mseed: int, vseed: int, f16: bool, flip: b
     for bi, b in enumerate(plan.blocks):
         segs = [trace[(bi, j)] for j in range(len(b.layers) + 1)]
         store = np.ascontiguousarray(torch.cat(segs, 1).round().to(torch.int8).numpy())
-        if hashed:
-            arrays[f"storehash_{bi}"] = np.frombuffer(table_hash(store).encode(), np.uint8)
+        if hashed:                       # one hash per image, [N][64] sha256 hex digits
+            arrays[f"storehash_{bi}"] = np.stack([np.frombuffer(table_hash(store[i]).encode(), np.uint8)
+                                                  for i in range(n)])
         else:
             arrays[f"store_{bi}"] = store
     if hashed:
