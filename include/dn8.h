@@ -68,15 +68,19 @@ int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream);
 
 /* conv2 of dense layer (b, l): replaces `conv2_t8x32_pl` / `conv2_t16x16_pl(C2Arg)` (reference
  * :2679-2832, `_c2_item` src/knee/dense8s.py:1274-1290). 3x3 pad-1 conv 128 -> 32 on the u8
- * bottleneck, q = rint(clamp(acc * sc_o, +-127)) written into the store slot [N][HW][32].
- * Requires W <= 128. */
+ * bottleneck, q = rint(clamp(acc * sc_o, +-127)) written into the store slot [N][HW][32] or, with
+ * tile_groups > 0, into group `group` of a tile-major block store. Requires W <= 128. */
 typedef struct dn8_conv2_args {
     const uint8_t* x;   /* bottleneck planes [8][N*H*W][16] */
     const int8_t* w;    /* L*_w2k [4][9][32][32] after dn8_prepare_conv2_weights (36864 bytes) */
     const float* sc;    /* L*_c2u: [32] float */
-    int8_t* out;        /* store slot [N][H*W][32] */
+    int8_t* out;        /* store slot [N][H*W][32], or the tile-major block store */
     int32_t* err;
     int32_t N, H, W;
+    /* 0: out is the slot. > 0: out is a tile-major block store [ceil(N*H*W/128)][tile_groups][128][32]
+     * (128 consecutive pixels per tile, all of a tile's groups contiguous) and this layer writes its
+     * group `group` (< tile_groups). */
+    int32_t tile_groups, group;
 } dn8_conv2_args;
 int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream);
 
@@ -96,6 +100,12 @@ typedef struct dn8_trans_args {
     int32_t* err;
     int32_t G0, G, N, H, W;
     int32_t prologue_f16;
+    /* > 0: in0 is a tile-major block store [ceil(N*H*W/128)][tile_groups][128][32] holding groups
+     * 0 .. G-1 (seg and G0 unused). */
+    int32_t tile_groups;
+    /* > 0: out is the next block's tile-major store [ceil(N*H*W/4/128)][out_tile_groups][128][32];
+     * the transition writes its groups 0 .. c_out/32 - 1. */
+    int32_t out_tile_groups;
 } dn8_trans_args;
 int dn8_trans(const dn8_trans_args* a, dn8_stream stream);
 
@@ -118,6 +128,9 @@ typedef struct dn8_stem_args {
     int32_t N, H, W;
     int32_t x_u8;
     int32_t n_alloc;       /* images the output groups are laid out for (>= N; 0 = N) */
+    /* > 0: out is block 1's tile-major store [ceil(n_alloc*H*W/16/128)][tile_groups][128][32]; the
+     * stem writes its groups 0 and 1. */
+    int32_t tile_groups;
 } dn8_stem_args;
 int dn8_stem(const dn8_stem_args* a, dn8_stream stream);
 
@@ -138,6 +151,9 @@ typedef struct dn8_head_args {
     int32_t* tickets;       /* [N / per_view] zero-initialised device counters (left zeroed) */
     int32_t G0, G, N, HW, n_out, per_view;
     int32_t n_alloc;        /* images the store groups are laid out for (>= N; 0 = N) */
+    /* > 0: in0 is the last block's tile-major store [ceil(n_alloc*HW/128)][tile_groups][128][32]
+     * holding groups 0 .. G-1 (seg and G0 unused). */
+    int32_t tile_groups;
 } dn8_head_args;
 int dn8_head(const dn8_head_args* a, dn8_stream stream);
 

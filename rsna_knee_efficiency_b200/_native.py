@@ -19,24 +19,25 @@ class Conv1Args(ctypes.Structure):
 
 class Conv2Args(ctypes.Structure):
     _fields_ = [("x", P), ("w", P), ("sc", P), ("out", P), ("err", P),
-                ("N", I32), ("H", I32), ("W", I32)]
+                ("N", I32), ("H", I32), ("W", I32), ("tile_groups", I32), ("group", I32)]
 
 
 class TransArgs(ctypes.Structure):
     _fields_ = [("in0", P), ("seg", P), ("w", P), ("ab", P), ("gd", P), ("out", P), ("err", P),
-                ("G0", I32), ("G", I32), ("N", I32), ("H", I32), ("W", I32), ("prologue_f16", I32)]
+                ("G0", I32), ("G", I32), ("N", I32), ("H", I32), ("W", I32), ("prologue_f16", I32),
+                ("tile_groups", I32), ("out_tile_groups", I32)]
 
 
 class StemArgs(ctypes.Structure):
     _fields_ = [("x", P), ("src", P), ("flags", P), ("w", P), ("kc", P), ("out", P), ("err", P),
-                ("N", I32), ("H", I32), ("W", I32), ("x_u8", I32), ("n_alloc", I32)]
+                ("N", I32), ("H", I32), ("W", I32), ("x_u8", I32), ("n_alloc", I32), ("tile_groups", I32)]
 
 
 class HeadArgs(ctypes.Structure):
     _fields_ = [("in0", P), ("seg", P), ("fab", P), ("feat", P), ("hw", P), ("hb", P),
                 ("logits", P), ("view_logits", P), ("tickets", P),
                 ("G0", I32), ("G", I32), ("N", I32), ("HW", I32), ("n_out", I32), ("per_view", I32),
-                ("n_alloc", I32)]
+                ("n_alloc", I32), ("tile_groups", I32)]
 
 
 class ZoomArgs(ctypes.Structure):

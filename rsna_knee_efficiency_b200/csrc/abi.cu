@@ -88,6 +88,9 @@ int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream) {
     if (a == nullptr) return fail(DN8_EINVAL, "dn8_conv2: null arguments");
     if (a->N < 1 || a->H < 1 || a->W < 1 || a->W > 128)
         return fail(DN8_EINVAL, "dn8_conv2: unsupported geometry N=%d H=%d W=%d (W <= 128)", a->N, a->H, a->W);
+    if (a->tile_groups < 0 || (a->tile_groups > 0 && (a->group < 0 || a->group >= a->tile_groups)))
+        return fail(DN8_EINVAL, "dn8_conv2: group %d outside the tile-major store's %d groups", a->group,
+                    a->tile_groups);
     if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->out) || a->sc == nullptr)
         return fail(DN8_EINVAL, "dn8_conv2: pointers must be non-null and 16-byte aligned");
     dn8::Conv2Plan plan;
@@ -105,8 +108,12 @@ int dn8_trans(const dn8_trans_args* a, dn8_stream stream) {
         a->W % 2)
         return fail(DN8_EINVAL, "dn8_trans: bad geometry G0=%d G=%d N=%d H=%d W=%d", a->G0, a->G, a->N, a->H, a->W);
     if (a->G * 16 > 640) return fail(DN8_EINVAL, "dn8_trans: c_out %d > 640", a->G * 16);
-    if (!aligned16(a->in0) || !aligned16(a->seg) || !aligned16(a->w) || !aligned16(a->ab) ||
-        !aligned16(a->out) || a->gd == nullptr)
+    if (a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G) || a->out_tile_groups < 0 ||
+        (a->out_tile_groups > 0 && a->out_tile_groups < a->G / 2))
+        return fail(DN8_EINVAL, "dn8_trans: tile-major stores of %d (in) / %d (out) groups cannot hold %d / %d",
+                    a->tile_groups, a->out_tile_groups, a->G, a->G / 2);
+    if (!aligned16(a->in0) || (a->tile_groups == 0 && !aligned16(a->seg)) || !aligned16(a->w) ||
+        !aligned16(a->ab) || !aligned16(a->out) || a->gd == nullptr)
         return fail(DN8_EINVAL, "dn8_trans: pointers must be non-null and 16-byte aligned");
     int sms = 0;
     if (int s = current_sms(&sms)) return s;
@@ -150,6 +157,8 @@ int dn8_stem(const dn8_stem_args* a, dn8_stream stream) {
                     a->H, a->W);
     if (a->x == nullptr || !aligned16(a->w) || a->kc == nullptr || !aligned16(a->out) || (a->x_u8 && a->src == nullptr))
         return fail(DN8_EINVAL, "dn8_stem: bad pointers");
+    if (a->tile_groups < 0 || a->tile_groups == 1)
+        return fail(DN8_EINVAL, "dn8_stem: a tile-major store needs at least the 2 groups the stem writes");
     int sms = 0;
     if (int s = current_sms(&sms)) return s;
     cudaError_t e = dn8::launch_stem(*a, sms, static_cast<cudaStream_t>(stream));
@@ -158,9 +167,10 @@ int dn8_stem(const dn8_stem_args* a, dn8_stream stream) {
 
 int dn8_head(const dn8_head_args* a, dn8_stream stream) {
     if (a == nullptr) return fail(DN8_EINVAL, "dn8_head: null arguments");
-    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64)
+    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64 ||
+        a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G))
         return fail(DN8_EINVAL, "dn8_head: bad geometry");
-    if (!aligned16(a->in0) || !aligned16(a->seg) || a->fab == nullptr)
+    if (!aligned16(a->in0) || (a->tile_groups == 0 && !aligned16(a->seg)) || a->fab == nullptr)
         return fail(DN8_EINVAL, "dn8_head: bad pointers");
     if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
         return fail(DN8_EINVAL, "dn8_head: head without bias or logits buffer");
@@ -192,9 +202,10 @@ int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
                     a->N / a->per_view, DN8_HEAD_SCRATCH_VIEWS);
     if (a->tickets != nullptr)
         return fail(DN8_EINVAL, "dn8_head_noalloc: tickets must be NULL (the built-in scratch is used)");
-    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64)
+    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64 ||
+        a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G))
         return fail(DN8_EINVAL, "dn8_head_noalloc: bad geometry");
-    if (!aligned16(a->in0) || !aligned16(a->seg) || a->fab == nullptr)
+    if (!aligned16(a->in0) || (a->tile_groups == 0 && !aligned16(a->seg)) || a->fab == nullptr)
         return fail(DN8_EINVAL, "dn8_head_noalloc: bad pointers");
     if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
         return fail(DN8_EINVAL, "dn8_head_noalloc: head without bias or logits buffer");

@@ -1,5 +1,6 @@
 // conv2.cu -- dense-layer conv2 on sm_100a: 3x3 pad-1 conv 128 -> 32 on the u8 bottleneck,
-// int8 requantisation straight into the block store slot.
+// int8 requantisation straight into the block store slot (the layer's [N][HW][32] segment, or its
+// group of a tile-major block store: pixel p at tile p / 128, row p % 128).
 //
 // Formulation ("dx in N"): a tile is Rt = 128 / W full image rows (128 pixels, W <= 128). For
 // each kernel row dy and channel block c (12 K steps of 32 channels) one
@@ -231,7 +232,11 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             const int tile = blockIdx.x + t * gridDim.x;
             const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
             if (yl < Rt && y0 + yl < H) {
-                int8_t* dst = a.out + ((static_cast<size_t>(n) * H + y0 + yl) * W + x) * 32 + ch * 16;
+                // pixel p of the slot [N][H*W][32], or group `group` of the tile-major block store
+                const size_t px = (static_cast<size_t>(n) * H + y0 + yl) * W + x;
+                int8_t* dst = a.tile_groups > 0
+                                  ? a.out + (((px >> 7) * a.tile_groups + a.group) << 12) + (px & 127) * 32 + ch * 16
+                                  : a.out + px * 32 + ch * 16;
                 *reinterpret_cast<uint4*>(dst) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
         };

@@ -4,8 +4,10 @@
 //     operand layouts once, and copied to the device in one allocation;
 //   * two alternating block arenas as in the reference (`_buffers`, dense8s.py:1073-1092): block b
 //     lives in arena b % 2 and its transition writes the next block's input into the other one.
-//     Every block store is group-major [G][n_cap][HW][32] (input groups first, then one group per
-//     dense layer), so segment l of block b is at group G0 + l;
+//     Every block store is tile-major [ceil(n_cap HW / 128)][Gt][128][32] (Gt = G0 + L groups: the
+//     block input groups first, then one group per dense layer; all groups of 128 consecutive pixels
+//     contiguous), so segment l of block b is group G0 + l of every tile and each conv1 stage reads
+//     one contiguous run;
 //   * a pass always runs the full capacity n_cap through the dense blocks (fixed shapes: a pass is
 //     capturable in a CUDA graph and its tensor maps stay valid); only the stem and the head see
 //     the real image count, so short batches cost one pass like the reference's padded blocks;
@@ -116,6 +118,15 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
     }
     if (p->h[0] * 4 != p->img || p->w[0] * 4 != p->img || p->c0[0] != 64)
         return bail(efail(e, DN8_EINVAL, "block 0 must be img/4 x img/4 with 64 input channels"));
+    for (int b = 0; b < p->n_blocks; ++b) {
+        // every block but the last ends in a transition that halves the map and the channels
+        const bool last = b == p->n_blocks - 1;
+        if (p->trans[b] != (last ? 0 : 1) ||
+            (!last && (p->c0[b + 1] * 2 != p->c0[b] + 32 * p->L[b] || p->h[b + 1] * 2 != p->h[b] ||
+                       p->w[b + 1] * 2 != p->w[b])))
+            return bail(efail(e, DN8_EINVAL, "block %d: transitions must chain the blocks (c0 = c_tot / 2, "
+                              "half the side) and the last block has none", b));
+    }
     HostTables ht;
     for (int i = 0; i < p->n_tables; ++i) ht.by_name[p->tables[i].name] = &p->tables[i];
 
@@ -208,7 +219,8 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
     for (int b = 0; b < e->n_blocks; ++b) {
         const size_t hwb = static_cast<size_t>(e->h[b]) * e->w[b];
         const size_t groups = e->c0[b] / 32 + e->L[b];
-        arena_bytes[b % 2] = std::max(arena_bytes[b % 2], groups * e->n * hwb * 32);
+        const size_t tiles = (static_cast<size_t>(e->n) * hwb + 127) / 128;
+        arena_bytes[b % 2] = std::max(arena_bytes[b % 2], tiles * groups * 4096);
         hw_max = std::max(hw_max, hwb);
     }
     bool ok = dev_alloc(reinterpret_cast<void**>(&e->tables), stage.size()) &&
@@ -286,49 +298,54 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
         s.flags = in->flags ? in->flags + img0 : nullptr;
         s.w = reinterpret_cast<const int8_t*>(e->sw); s.kc = e->kc; s.out = e->arena[0]; s.err = e->err;
         s.N = n; s.H = e->img; s.W = e->img; s.x_u8 = in->x_u8; s.n_alloc = cap;
+        s.tile_groups = e->c0[0] / 32 + e->L[0];
         if ((ce = dn8::launch_stem(s, e->sms, st)) != cudaSuccess) return efail(e, DN8_ECUDA, "stem: %s", cudaGetErrorString(ce));
         mark(e, DN8_K_STEM, 0, 0, st);
     }
     for (int b = 0; b < e->n_blocks; ++b) {
-        const int HW = e->h[b] * e->w[b], G0 = e->c0[b] / 32;
-        int8_t* in0 = e->arena[b % 2];
-        int8_t* seg = in0 + static_cast<size_t>(G0) * cap * HW * 32;
+        const int HW = e->h[b] * e->w[b], G0 = e->c0[b] / 32, Gt = G0 + e->L[b];
+        int8_t* store = e->arena[b % 2];                 // tile-major [tiles][Gt][128][32]
         for (int l = 0; l < e->L[b]; ++l) {
             const dn8_engine::Layer& ly = e->layers[b][l];
             dn8_conv1_args c1{};
-            c1.in0 = in0; c1.seg = seg; c1.w = reinterpret_cast<const int8_t*>(ly.w1); c1.ab = ly.ab; c1.gd = ly.gd;
+            c1.in0 = store; c1.seg = nullptr; c1.w = reinterpret_cast<const int8_t*>(ly.w1); c1.ab = ly.ab; c1.gd = ly.gd;
             c1.out = e->bott; c1.err = e->err; c1.G0 = G0; c1.G = G0 + l; c1.N = cap; c1.HW = HW;
             c1.prologue_f16 = e->c1_f16[b][l];
+            c1.tile_groups = Gt;
             if ((ce = dn8::launch_conv1(c1, e->sms, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv1 b%d l%d: %s", b, l, cudaGetErrorString(ce));
             mark(e, DN8_K_CONV1, b, l, st);
             dn8_conv2_args c2{};
             c2.x = e->bott; c2.w = reinterpret_cast<const int8_t*>(ly.w2); c2.sc = ly.c2;
-            c2.out = seg + static_cast<size_t>(l) * cap * HW * 32; c2.err = e->err;
+            c2.out = store; c2.err = e->err;
             c2.N = cap; c2.H = e->h[b]; c2.W = e->w[b];
+            c2.tile_groups = Gt; c2.group = G0 + l;
             if ((ce = dn8::launch_conv2(e->c2plan[b], c2, e->sms, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv2 b%d l%d: %s", b, l, cudaGetErrorString(ce));
             mark(e, DN8_K_CONV2, b, l, st);
         }
         if (e->trans[b]) {
             dn8_trans_args t{};
-            t.in0 = in0; t.seg = seg; t.w = reinterpret_cast<const int8_t*>(e->tw[b]); t.ab = e->tab[b]; t.gd = e->tgd[b];
+            t.in0 = store; t.seg = nullptr; t.w = reinterpret_cast<const int8_t*>(e->tw[b]); t.ab = e->tab[b]; t.gd = e->tgd[b];
             t.out = e->arena[(b + 1) % 2]; t.err = e->err;
-            t.G0 = G0; t.G = G0 + e->L[b]; t.N = cap; t.H = e->h[b]; t.W = e->w[b]; t.prologue_f16 = e->trans_f16[b];
+            t.G0 = G0; t.G = Gt; t.N = cap; t.H = e->h[b]; t.W = e->w[b]; t.prologue_f16 = e->trans_f16[b];
+            t.tile_groups = Gt;
+            t.out_tile_groups = e->c0[b + 1] / 32 + e->L[b + 1];
             if ((ce = dn8::launch_trans(t, e->sms, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "transition %d: %s", b, cudaGetErrorString(ce));
             mark(e, DN8_K_TRANS, b, 0, st);
         } else {
             dn8_head_args hd{};
-            hd.in0 = in0; hd.seg = seg; hd.fab = e->fab;
-            const int C = (G0 + e->L[b]) * 32;
+            hd.in0 = store; hd.seg = nullptr; hd.fab = e->fab;
+            hd.tile_groups = Gt;
+            const int C = Gt * 32;
             hd.feat = feat ? feat + static_cast<size_t>(img0) * C : nullptr;
             hd.hw = e->hw; hd.hb = e->hb;
             hd.logits = (e->hw && logits) ? logits + static_cast<size_t>(img0) * e->n_out : nullptr;
             if (hd.logits == nullptr) hd.hw = nullptr;
             hd.view_logits = (hd.hw && view_logits && per_view > 0) ? view_logits + static_cast<size_t>(img0 / per_view) * e->n_out : nullptr;
             hd.tickets = e->tickets;
-            hd.G0 = G0; hd.G = G0 + e->L[b]; hd.N = n; hd.HW = HW; hd.n_out = e->n_out; hd.per_view = per_view;
+            hd.G0 = G0; hd.G = Gt; hd.N = n; hd.HW = HW; hd.n_out = e->n_out; hd.per_view = per_view;
             hd.n_alloc = cap;
             if ((ce = dn8::launch_head(hd, st, true)) != cudaSuccess) return efail(e, DN8_ECUDA, "head: %s", cudaGetErrorString(ce));
             mark(e, DN8_K_HEAD, b, 0, st);
@@ -403,12 +420,23 @@ int dn8_engine_store(const dn8_engine* ec, int32_t block, int32_t j, int8_t* dst
     dn8_engine* e = const_cast<dn8_engine*>(ec);
     if (e == nullptr || block < 0 || block >= e->n_blocks || j < 0 || j > e->L[block] || dst == nullptr)
         return efail(e, DN8_EINVAL, "store: bad arguments");
-    const size_t HW = static_cast<size_t>(e->h[block]) * e->w[block];
-    const int G0 = e->c0[block] / 32;
+    const size_t rows = static_cast<size_t>(e->n) * e->h[block] * e->w[block];
+    const size_t full = rows / 128, rest = rows % 128;             // whole tiles, rows of the last one
+    const int G0 = e->c0[block] / 32, Gt = G0 + e->L[block];
     const int8_t* base = e->arena[block % 2];
-    const size_t bytes = (j == 0 ? G0 : 1) * static_cast<size_t>(e->n) * HW * 32;
-    const int8_t* src = j == 0 ? base : base + (static_cast<size_t>(G0) + j - 1) * e->n * HW * 32;
-    cudaError_t ce = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // group g of the tile-major store [tiles][Gt][128][32] -> rows x 32 bytes at dst, per group:
+    // the whole tiles as one strided copy (4 KB per tile, Gt * 4 KB apart), then the partial last tile
+    cudaError_t ce = cudaSuccess;
+    const int g0 = j == 0 ? 0 : G0 + j - 1, ng = j == 0 ? G0 : 1;
+    for (int g = g0; g < g0 + ng && ce == cudaSuccess; ++g) {
+        int8_t* d = dst + static_cast<size_t>(g - g0) * rows * 32;
+        const int8_t* sg = base + static_cast<size_t>(g) * 4096;
+        if (full > 0)
+            ce = cudaMemcpy2DAsync(d, 4096, sg, static_cast<size_t>(Gt) * 4096, 4096, full, cudaMemcpyDefault, st);
+        if (ce == cudaSuccess && rest > 0)
+            ce = cudaMemcpyAsync(d + full * 4096, sg + full * Gt * 4096, rest * 32, cudaMemcpyDefault, st);
+    }
     return ce == cudaSuccess ? DN8_OK : efail(e, DN8_ECUDA, "store: %s", cudaGetErrorString(ce));
 }
 

@@ -72,7 +72,8 @@ struct GemmArgs {
     int sb;                   // weight ring stages when streamed
     int raw_bytes;            // raw ring slot size (a whole stage)
     int sr;                   // raw ring slots
-    int tg;                   // conv1: 0 = group-major planes; > 0 = tile-major store with tg groups per tile
+    int tg;                   // 0 = group-major planes; > 0 = tile-major input store with tg groups per tile
+    int tg_out;               // transition: 0 = group-major output; > 0 = the next block's tile-major store
 };
 
 // Byte range [first, end) of the flattened input pixels (n * HW + y * W + x) a transition tile of
@@ -305,11 +306,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int cnt = min(128, rows - m0);               // pair: <= 0 past the last rows
             size_t off;
             uint32_t bytes;
+            int ntl = 0;                                       // transition, tile-major: tiles of the span
             if (TRANS) {
                 int first, end;
                 trans_span(m0, cnt, HW, a.W, &first, &end);
-                off = static_cast<size_t>(first) * 32;
-                bytes = static_cast<uint32_t>(end - first) * 32;
+                if (a.tg > 0) {
+                    // whole 4 KB tiles first / 128 .. (end - 1) / 128 of each K group
+                    off = static_cast<size_t>(first >> 7) * a.tg * 4096;
+                    ntl = ((end - 1) >> 7) - (first >> 7) + 1;
+                    bytes = static_cast<uint32_t>(ntl) * 4096u;
+                } else {
+                    off = static_cast<size_t>(first) * 32;
+                    bytes = static_cast<uint32_t>(end - first) * 32;
+                }
             } else if (a.tg > 0) {
                 // tile-major: a stage is the tile's groups j*KSTEP .. in one contiguous run of 4 KB each
                 // (whole 128-row tiles are allocated, so a partial last tile is copied whole)
@@ -329,7 +338,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     if (ok) mbar_expect_tx(&fullR[s], bytes * gc);
                 }
                 if (!__shfl_sync(0xffffffffu, ok, 0)) { ok_run = false; break; }
-                if (!TRANS && a.tg > 0) {
+                if (TRANS && a.tg > 0) {
+                    // one 4 KB copy per tile of the span, tiles tg groups apart
+                    if (lane < ntl)
+                        bulk_g2s(sR + s * RB + lane * 4096,
+                                 a.in0 + off + (static_cast<size_t>(lane) * a.tg + j) * 4096, 4096u, &fullR[s]);
+                } else if (!TRANS && a.tg > 0) {
                     if (lane == 0 && bytes > 0)
                         bulk_g2s(sR + s * RB, a.in0 + off + static_cast<size_t>(j) * KSTEP * 4096,
                                  static_cast<uint32_t>(gc) * 4096u, &fullR[s]);
@@ -466,11 +480,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 const int tile = unit + t * nunits;
                 const int m0 = (tile / a.nchunks) * 128;
                 const int gr0 = m0 / W2;
+                const int first = 2 * W * gr0;                    // first input pixel of the copied span
                 int m = min(m0 + (lane >> 1), rows - 1);
                 int gr = m / W2, ox = m - gr * W2;
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
-                    off[jj] = (2 * W * (gr - gr0) + (x >> 1) * W + 2 * ox + (x & 1)) * 32 + h * 16;
+                    const int rel = 2 * W * (gr - gr0) + (x >> 1) * W + 2 * ox + (x & 1);
+                    if (a.tg > 0) {                               // tile-major span: whole 4 KB tiles
+                        const int q = first + rel;
+                        off[jj] = ((q >> 7) - (first >> 7)) * 4096 + (q & 127) * 32 + h * 16;
+                    } else {
+                        off[jj] = rel * 32 + h * 16;
+                    }
                     if (jj < 7) {                         // next chunk row: +16 pooled pixels
                         const int step = min(16, rows - 1 - m);
                         m += step;
@@ -577,10 +598,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 }
                 if (m < rows) {
                     uint8_t* o = static_cast<uint8_t*>(a.out);
-                    // transition: next block input, group-major [c_out / 32][N * HW / 4][32];
-                    // conv1: bottleneck planes of 16 channels [8][N * HW][16]
-                    const size_t off = TRANS ? (static_cast<size_t>(c0 >> 5) * rows + m) * 32 + (c0 & 16)
-                                             : (static_cast<size_t>(c0 >> 4) * rows + m) * 16;
+                    // transition: next block input, group-major [c_out / 32][N * HW / 4][32] or groups
+                    // 0 .. c_out / 32 - 1 of its tile-major store; conv1: bottleneck planes of 16
+                    // channels [8][N * HW][16]
+                    size_t off;
+                    if (TRANS && a.tg_out > 0)
+                        off = ((static_cast<size_t>(m >> 7) * a.tg_out + (c0 >> 5)) << 12) + (m & 127) * 32 + (c0 & 16);
+                    else if (TRANS)
+                        off = (static_cast<size_t>(c0 >> 5) * rows + m) * 32 + (c0 & 16);
+                    else
+                        off = (static_cast<size_t>(c0 >> 4) * rows + m) * 16;
                     *reinterpret_cast<uint4*>(o + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
                 }
             };
@@ -715,9 +742,15 @@ int trans_chunk(int cout) { return cout >= 256 ? 256 : 128; }
 // Largest raw span of a transition tile: its 128 consecutive pooled pixels cover at most
 // 128 / W2 pooled rows when W2 divides 128 (tiles start on a row), else ceil(128 / W2) + 1;
 // each pooled row needs two whole input rows.
-static int trans_raw_bytes(int W) {
+static int trans_raw_bytes(int W, bool tiled) {
     const int W2 = W / 2;
     const int prow = (128 % W2 == 0) ? 128 / W2 : (128 + W2 - 1) / W2 + 1;
+    if (tiled) {
+        // whole 4 KB tiles: a span of 2 prow W pixels starting anywhere covers at most this many,
+        // exactly 2 prow W / 128 when the span starts on a tile (W / 2 divides 128: every block at 512 px)
+        const int span = 2 * prow * W;
+        return (128 % W2 == 0 && span % 128 == 0 ? span / 128 : span / 128 + 2) * 4096;
+    }
     return ((2 * prow * W * 32 + 1023) / 1024) * 1024;
 }
 
@@ -729,7 +762,9 @@ cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st, bool
     g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.H * a.W; g.W = a.W;
     g.rows = a.N * (a.H / 2) * (a.W / 2); g.cout = cout; g.nc = trans_chunk(cout);
     g.nchunks = (cout + g.nc - 1) / g.nc;
-    g.raw_bytes = trans_raw_bytes(a.W);
+    g.raw_bytes = trans_raw_bytes(a.W, a.tile_groups > 0);
+    g.tg = a.tile_groups;
+    g.tg_out = a.out_tile_groups;
     return a.prologue_f16 ? launch_gemm<true, true>(g, sms, st, pdl) : launch_gemm<false, true>(g, sms, st, pdl);
 }
 

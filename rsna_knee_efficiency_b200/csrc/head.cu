@@ -28,9 +28,18 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
     // task = (group g, half h, partial q): 16 channels, pixels q, q + 4, ...
     for (int task = tid; task < a.G * 8; task += HD_THREADS) {
         const int g = task >> 3, h = (task >> 2) & 1, q = task & 3;
-        const int8_t* base = g < a.G0 ? a.in0 + ((static_cast<size_t>(g) * nal + n) * HW) * 32
-                                      : a.seg + ((static_cast<size_t>(g - a.G0) * nal + n) * HW) * 32;
-        base += h * 16;
+        // pixel s of image n in group g: group-major planes, or the tile-major store (pixel p = n HW + s
+        // at tile p / 128, row p % 128)
+        const int8_t* base;
+        size_t tstride = 0, p0 = 0;
+        if (a.tile_groups > 0) {
+            base = a.in0 + static_cast<size_t>(g) * 4096 + h * 16;
+            tstride = static_cast<size_t>(a.tile_groups) << 12;
+            p0 = static_cast<size_t>(n) * HW;
+        } else {
+            base = (g < a.G0 ? a.in0 + ((static_cast<size_t>(g) * nal + n) * HW) * 32
+                             : a.seg + ((static_cast<size_t>(g - a.G0) * nal + n) * HW) * 32) + h * 16;
+        }
         const float2* ab = reinterpret_cast<const float2*>(a.fab) + g * 32 + h * 16;
         float av[16], bv[16], acc[16];
 #pragma unroll
@@ -44,7 +53,9 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
         // ascending pixel order)
 #pragma unroll 4
         for (int s = q; s < HW; s += 4) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + static_cast<size_t>(s) * 32));
+            const size_t p = p0 + s;
+            const int8_t* src = a.tile_groups > 0 ? base + (p >> 7) * tstride + (p & 127) * 32 : base + p * 32;
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
             const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
 #pragma unroll
             for (int k = 0; k < 16; ++k) {

@@ -1,7 +1,8 @@
 // stem.cu -- the INT8 stem on sm_100a, fused with the input producer: pixels -> u8 (the uint8
 // volume planes directly, or rint(255 sat(x)) of fp16 windows), optional horizontal flip, 7x7/2
 // pad-3 conv 3 -> 64 on tcgen05 (kind::i8), q = rint(clamp(fmaf(acc, k, c), 0, 127)), 3x3/2 pad-1
-// max-pool on the bytes, into block 1's group-major input [2][N][H/4 * W/4][32].
+// max-pool on the bytes, into block 1's group-major input [2][N][H/4 * W/4][32] or groups 0-1 of
+// its tile-major store.
 // Arithmetic of the reference's `stem_i8_body` (src/knee/dense8s_kernels.cu:3641-3771) and
 // `stem_q_i8` (src/knee/dense8s.py:625-643).
 //
@@ -398,9 +399,12 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                                 }
                             }
                         }
-                        // block 1 input, group-major [2][N][PH * PW][32]: this half is group pxh
+                        // block 1 input, group-major [2][N][PH * PW][32] (this half is group pxh), or
+                        // groups 0 / 1 of the tile-major block store
                         const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
-                        int8_t* o = a.out + pxh * gstride + pix * 32;
+                        int8_t* o = a.tile_groups > 0
+                                        ? a.out + (((pix >> 7) * a.tile_groups + pxh) << 12) + (pix & 127) * 32
+                                        : a.out + pxh * gstride + pix * 32;
                         uint32_t mx[8];
 #pragma unroll
                         for (int j = 0; j < 8; ++j) mx[j] = __byte_perm(mxe[j], mxo[j], 0x6240);

@@ -1,8 +1,9 @@
 """Kernel-level operators on torch CUDA tensors (the reference's per-kernel launches, through the
 C ABI of include/dn8.h). Layouts:
-  store  in0 [N, G0, HW, 32] int8, seg [L, N, HW, 32] int8 (the reference's block store);
+  store  group-major in0 [G0, N, HW, 32] int8 and seg [L, N, HW, 32] int8, or (tile_groups = Gt > 0)
+         the tile-major block store [ceil(N*HW/128), Gt, 128, 32] int8 holding every group;
   bottleneck u8 as 8 planes of 16 channels [8, N*HW, 16];
-  conv2 output: the store slot [N, HW, 32] int8.
+  conv2 output: the store slot [N, HW, 32] int8, or group `group` of a tile-major store.
 """
 from __future__ import annotations
 
@@ -31,36 +32,36 @@ def conv1(in0: torch.Tensor, seg: torch.Tensor | None, w1: torch.Tensor, ab: tor
 
 
 def conv2(x: torch.Tensor, w2k: torch.Tensor, sc: torch.Tensor, out: torch.Tensor, N: int, H: int,
-          W: int, err: torch.Tensor | None = None, stream=None) -> None:
-    a = nat.Conv2Args(_ptr(x), _ptr(w2k), _ptr(sc), _ptr(out), _ptr(err), N, H, W)
+          W: int, err: torch.Tensor | None = None, stream=None, tile_groups: int = 0, group: int = 0) -> None:
+    a = nat.Conv2Args(_ptr(x), _ptr(w2k), _ptr(sc), _ptr(out), _ptr(err), N, H, W, tile_groups, group)
     nat.check(nat.lib().dn8_conv2(a, _stream(stream)), "dn8_conv2")
 
 
 def trans(in0: torch.Tensor, seg: torch.Tensor, tw: torch.Tensor, ab: torch.Tensor, gd: torch.Tensor,
           out: torch.Tensor, G0: int, G: int, N: int, H: int, W: int, prologue_f16: bool,
-          err: torch.Tensor | None = None, stream=None) -> None:
+          err: torch.Tensor | None = None, stream=None, tile_groups: int = 0, out_tile_groups: int = 0) -> None:
     a = nat.TransArgs(_ptr(in0), _ptr(seg), _ptr(tw), _ptr(ab), _ptr(gd), _ptr(out), _ptr(err),
-                      G0, G, N, H, W, int(bool(prologue_f16)))
+                      G0, G, N, H, W, int(bool(prologue_f16)), tile_groups, out_tile_groups)
     nat.check(nat.lib().dn8_trans(a, _stream(stream)), "dn8_trans")
 
 
 def stem(x: torch.Tensor, w8u: torch.Tensor, kc: torch.Tensor, out: torch.Tensor, N: int, H: int,
          W: int, src: torch.Tensor | None = None, flags: torch.Tensor | None = None,
-         err: torch.Tensor | None = None, stream=None) -> None:
+         err: torch.Tensor | None = None, stream=None, tile_groups: int = 0) -> None:
     """x: fp16 [N, 3, H, W] windows, or uint8 planes [P, H, W] with `src` int32 [N, 4]."""
     x_u8 = x.dtype == torch.uint8
     a = nat.StemArgs(_ptr(x), _ptr(src), _ptr(flags), _ptr(w8u), _ptr(kc), _ptr(out), _ptr(err),
-                     N, H, W, int(x_u8), 0)
+                     N, H, W, int(x_u8), 0, tile_groups)
     nat.check(nat.lib().dn8_stem(a, _stream(stream)), "dn8_stem")
 
 
 def head(in0: torch.Tensor, seg: torch.Tensor, fab: torch.Tensor, G0: int, G: int, N: int, HW: int,
          feat: torch.Tensor | None = None, hw: torch.Tensor | None = None, hb: torch.Tensor | None = None,
          logits: torch.Tensor | None = None, view_logits: torch.Tensor | None = None,
-         tickets: torch.Tensor | None = None, per_view: int = 0, stream=None) -> None:
+         tickets: torch.Tensor | None = None, per_view: int = 0, stream=None, tile_groups: int = 0) -> None:
     n_out = 0 if hw is None else hw.shape[0]
     a = nat.HeadArgs(_ptr(in0), _ptr(seg), _ptr(fab), _ptr(feat), _ptr(hw), _ptr(hb), _ptr(logits),
-                     _ptr(view_logits), _ptr(tickets), G0, G, N, HW, n_out, per_view, 0)
+                     _ptr(view_logits), _ptr(tickets), G0, G, N, HW, n_out, per_view, 0, tile_groups)
     nat.check(nat.lib().dn8_head(a, _stream(stream)), "dn8_head")
 
 

@@ -53,3 +53,22 @@ def pixels_to_planes(v: np.ndarray) -> np.ndarray:
 
 def dev(a: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def tile_major(X: np.ndarray, Gt: int | None = None) -> np.ndarray:
+    """Channel-last store X [N, HW, c] (c = 32 G) -> the tile-major block store
+    [ceil(N HW / 128), Gt, 128, 32] (groups G .. Gt - 1 and the rows past the last pixel zero)."""
+    N, HW, c = X.shape
+    G = c // 32
+    Gt = G if Gt is None else Gt
+    rows = N * HW
+    nt = -(-rows // 128)
+    t = np.zeros((nt * 128, Gt, 32), np.int8)
+    t[:rows, :G] = X.reshape(rows, G, 32)
+    return np.ascontiguousarray(t.reshape(nt, 128, Gt, 32).transpose(0, 2, 1, 3))
+
+
+def from_tile_major(t: np.ndarray, rows: int, groups) -> np.ndarray:
+    """Tile-major [T, Gt, 128, 32] -> channel-last [rows, 32 len(groups)] of the given groups."""
+    flat = t.transpose(0, 2, 1, 3).reshape(-1, t.shape[1], 32)[:rows]
+    return np.ascontiguousarray(flat[:, list(groups)].reshape(rows, -1))
