@@ -233,6 +233,18 @@ int dn8_engine_forward(dn8_engine* e, const dn8_input* in, int32_t n, float* fea
 /* Synchronises `stream`, then reads (and clears) the device error word: DN8_EDEVICE if a kernel gave
  * up a bounded wait since the last check. */
 int dn8_engine_check(dn8_engine* e, dn8_stream stream);
+/* Enqueues one pass of n (<= pass size) images that stops after the dense layers of block
+ * `last_block` (its transition and, for the last block, the pooling + head are not run), so that
+ * dn8_engine_store reads blocks last_block - 1 and last_block as the pass left them. The reference's
+ * `Dense8SEncoder.trace` (src/knee/dense8s.py:1509-1546) copies the store after every block; passes
+ * are deterministic, so a partial pass and a full one give every block's store. */
+int dn8_engine_forward_to(dn8_engine* e, const dn8_input* in, int32_t n, int32_t last_block, dn8_stream stream);
+/* Launches one kernel of a pass -- kind DN8_K_CONV1 or DN8_K_CONV2 of dense layer `layer` of block
+ * `block`, or DN8_K_TRANS of block `block` -- on the engine's arenas exactly as a pass does, without
+ * programmatic dependence on the previous launch. For timing (the reference's `time_layers` times
+ * its stored launch items, src/knee/dense8s.py:1583-1596): it reads whatever the last pass left
+ * and overwrites what that kernel writes. No allocation, no synchronisation. */
+int dn8_engine_launch(dn8_engine* e, int32_t kind, int32_t block, int32_t layer, dn8_stream stream);
 /* Copies store segment j of block b (j = 0: the block input groups [G0][n][HW][32]; j >= 1: the
  * output of dense layer j-1, [n][HW][32]) to dst (device or host memory). Valid for the last two
  * blocks of the last pass (blocks alternate between two arenas). */
@@ -253,6 +265,16 @@ int dn8_engine_profile(dn8_engine* e, const dn8_input* in, int32_t n, float* fea
                        int32_t max_out, int32_t* n_launches, dn8_stream stream);
 const char* dn8_engine_error(const dn8_engine* e);
 int64_t dn8_engine_device_bytes(const dn8_engine* e);
+
+/* ---- test hook (failure detection without a GPU fault) -------------------------------------
+ * Arms the next dn8_conv1 launch of the process (kernel level or inside an engine pass) with a short
+ * wait limit (`wait_limit_cycles` SM cycles instead of ~2^32) and, for fault = 1, makes the store
+ * producer of its first CTA (or CTA pair) announce raw stage 0 of its first tile but never copy it.
+ * That CTA's consumers then give up their bounded wait: the launch sets its error word (a dn8_conv1
+ * `err` array, or the engine's: dn8_engine_check returns DN8_EDEVICE), every role leaves its loop,
+ * the kernel frees its tensor memory and returns, and the context stays usable. fault = 0 disarms.
+ * No counterpart in the reference; never armed outside tests. */
+int dn8_test_inject_wait_fault(int32_t fault, int64_t wait_limit_cycles);
 
 const char* dn8_last_error(void);   /* message of the calling thread's last failed call */
 int dn8_device_sms(int device);     /* SM count used to size persistent grids (0 on error) */

@@ -7,6 +7,7 @@ import ctypes
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libdn8b200.so")
+IN_TREE = LIB_PATH
 DN8_OK, DN8_EINVAL, DN8_ECUDA, DN8_EDEVICE = 0, 1, 2, 3
 DN8_HEAD_SCRATCH_VIEWS = 4096
 P, I32 = ctypes.c_void_p, ctypes.c_int32
@@ -66,6 +67,7 @@ class LaunchInfo(ctypes.Structure):
 
 
 KIND_NAMES = {0: "stem", 1: "conv1", 2: "conv2", 3: "trans", 4: "head"}
+K_STEM, K_CONV1, K_CONV2, K_TRANS, K_HEAD = 0, 1, 2, 3, 4
 
 EXPORTS = {
     "dn8_conv1": ([ctypes.POINTER(Conv1Args), P], ctypes.c_int),
@@ -86,8 +88,11 @@ EXPORTS = {
     "dn8_engine_profile": ([P, ctypes.POINTER(Input), I32, P, ctypes.POINTER(LaunchInfo), I32,
                             ctypes.POINTER(I32), P], ctypes.c_int),
     "dn8_engine_store": ([P, I32, I32, P, P], ctypes.c_int),
+    "dn8_engine_forward_to": ([P, ctypes.POINTER(Input), I32, I32, P], ctypes.c_int),
+    "dn8_engine_launch": ([P, I32, I32, I32, P], ctypes.c_int),
     "dn8_engine_error": ([P], ctypes.c_char_p),
     "dn8_engine_device_bytes": ([P], ctypes.c_int64),
+    "dn8_test_inject_wait_fault": ([I32, ctypes.c_int64], ctypes.c_int),
     "dn8_last_error": ([], ctypes.c_char_p),
     "dn8_device_sms": ([ctypes.c_int], ctypes.c_int),
 }
@@ -104,6 +109,8 @@ def lib():
                                "`python -m rsna_knee_efficiency_b200.build` (no CPU fallback)")
         handle = ctypes.CDLL(str(LIB_PATH))
         for name, (args, res) in EXPORTS.items():
+            if LIB_PATH != IN_TREE and not hasattr(handle, name):
+                continue                 # another build (bench.py --lib) may predate newer entry points
             fn = getattr(handle, name)
             fn.argtypes, fn.restype = args, res
         _lib = handle

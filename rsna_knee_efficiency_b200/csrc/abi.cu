@@ -222,6 +222,13 @@ int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
     return e == cudaSuccess ? DN8_OK : cuda_fail(e, "dn8_head_noalloc launch");
 }
 
+int dn8_test_inject_wait_fault(int32_t fault, int64_t wait_limit_cycles) {
+    if (fault < 0 || fault > 1 || wait_limit_cycles < 0 || (fault == 1 && wait_limit_cycles == 0))
+        return fail(DN8_EINVAL, "dn8_test_inject_wait_fault: fault 0 or 1 (with a wait limit > 0)");
+    dn8::arm_wait_fault(fault, wait_limit_cycles);
+    return DN8_OK;
+}
+
 int dn8_prepare_stem_weights(const int8_t* w8, uint8_t* out) {
     if (w8 == nullptr || out == nullptr) return fail(DN8_EINVAL, "dn8_prepare_stem_weights: bad arguments");
     // S_w8 [64][176] (k = (ch * 7 + ky) * 8 + kx') -> 7 K steps, one per kernel row ky, of

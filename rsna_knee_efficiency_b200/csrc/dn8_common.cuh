@@ -63,14 +63,15 @@ DN8_DEV bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(ns) : "memory");
     return ok != 0;
 }
-// Waits for the phase of parity `parity` to complete. Returns false (error raised) on timeout or
-// when another role has already aborted.
-DN8_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code) {
+// Waits for the phase of parity `parity` to complete. Returns false (error raised) on timeout (after
+// `limit` SM cycles) or when another role has already aborted.
+DN8_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code,
+                       long long limit = WAIT_LIMIT) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_sleep(bar, parity, 100000u)) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > WAIT_LIMIT) {
+        if (clock64() - t0 > limit) {
             raise_error(err, abort_flag, code);
             return false;
         }
@@ -211,8 +212,9 @@ DN8_DEV void umma_commit_pair_w(uint64_t* bar) {
 }
 // Every lane waits; the warp continues only if all of them saw the phase (a timeout or an abort seen
 // by any lane stops the whole warp, so the issuing loop stays converged).
-DN8_DEV bool mbar_wait_w(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code) {
-    return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, abort_flag, code)) != 0;
+DN8_DEV bool mbar_wait_w(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag, int code,
+                         long long limit = WAIT_LIMIT) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, abort_flag, code, limit)) != 0;
 }
 // tcgen05.ld writes its registers asynchronously: their values may be read only after
 // tcgen05.wait::ld. A wait with a "memory" clobber alone orders memory, not registers, so the compiler

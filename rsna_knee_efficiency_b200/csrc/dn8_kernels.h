@@ -50,6 +50,7 @@ cudaError_t launch_pdl_pairs(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3
 __attribute__((visibility("hidden"))) void set_last_error(const char* msg);  // thread-local message (abi.cu)
 
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool pdl = false);
+void arm_wait_fault(int fault, long long wait_limit);   // test hook of the next conv1 launch
 bool conv1_supported(int G);   // the layer's weights fit (resident) on single CTAs or CTA pairs
 cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st, bool pdl = false);
 int trans_chunk(int cout);

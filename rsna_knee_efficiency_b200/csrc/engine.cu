@@ -284,9 +284,46 @@ static void mark(dn8_engine* e, int kind, int block, int layer, cudaStream_t st)
     e->rec.push_back({kind, block, layer, 0.0f});
 }
 
-// One pass of up to n_cap images (images [0, n) of the pass are real).
+// The dense-layer and transition launches of a pass, on the engine's arenas (pdl: programmatic
+// dependent launch on the previous kernel of the pass).
+static cudaError_t launch_conv1_of(dn8_engine* e, int b, int l, cudaStream_t st, bool pdl) {
+    const int G0 = e->c0[b] / 32;
+    const dn8_engine::Layer& ly = e->layers[b][l];
+    dn8_conv1_args c1{};
+    c1.in0 = e->arena[b % 2]; c1.seg = nullptr; c1.w = reinterpret_cast<const int8_t*>(ly.w1); c1.ab = ly.ab;
+    c1.gd = ly.gd; c1.out = e->bott; c1.err = e->err; c1.G0 = G0; c1.G = G0 + l; c1.N = e->n;
+    c1.HW = e->h[b] * e->w[b]; c1.prologue_f16 = e->c1_f16[b][l];
+    c1.tile_groups = G0 + e->L[b];
+    return dn8::launch_conv1(c1, e->sms, st, pdl);
+}
+
+static cudaError_t launch_conv2_of(dn8_engine* e, int b, int l, cudaStream_t st, bool pdl) {
+    const int G0 = e->c0[b] / 32;
+    const dn8_engine::Layer& ly = e->layers[b][l];
+    dn8_conv2_args c2{};
+    c2.x = e->bott; c2.w = reinterpret_cast<const int8_t*>(ly.w2); c2.sc = ly.c2;
+    c2.out = e->arena[b % 2]; c2.err = e->err;
+    c2.N = e->n; c2.H = e->h[b]; c2.W = e->w[b];
+    c2.tile_groups = G0 + e->L[b]; c2.group = G0 + l;
+    return dn8::launch_conv2(e->c2plan[b], c2, e->sms, st, pdl);
+}
+
+static cudaError_t launch_trans_of(dn8_engine* e, int b, cudaStream_t st, bool pdl) {
+    const int G0 = e->c0[b] / 32, Gt = G0 + e->L[b];
+    dn8_trans_args t{};
+    t.in0 = e->arena[b % 2]; t.seg = nullptr; t.w = reinterpret_cast<const int8_t*>(e->tw[b]); t.ab = e->tab[b];
+    t.gd = e->tgd[b]; t.out = e->arena[(b + 1) % 2]; t.err = e->err;
+    t.G0 = G0; t.G = Gt; t.N = e->n; t.H = e->h[b]; t.W = e->w[b]; t.prologue_f16 = e->trans_f16[b];
+    t.tile_groups = Gt;
+    t.out_tile_groups = e->c0[b + 1] / 32 + e->L[b + 1];
+    return dn8::launch_trans(t, e->sms, st, pdl);
+}
+
+// One pass of up to n_cap images (images [0, n) of the pass are real), through dense block
+// `last_block`: its transition (or, for the last block, the pooling + head) runs only when the pass
+// goes past it.
 static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, float* feat, float* logits,
-                       float* view_logits, int per_view, cudaStream_t st) {
+                       float* view_logits, int per_view, cudaStream_t st, int last_block = 1 << 30) {
     const int cap = e->n;
     cudaError_t ce;
     // stem -> block 0 input groups (arena 0)
@@ -302,41 +339,24 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
         if ((ce = dn8::launch_stem(s, e->sms, st)) != cudaSuccess) return efail(e, DN8_ECUDA, "stem: %s", cudaGetErrorString(ce));
         mark(e, DN8_K_STEM, 0, 0, st);
     }
-    for (int b = 0; b < e->n_blocks; ++b) {
+    for (int b = 0; b < e->n_blocks && b <= last_block; ++b) {
         const int HW = e->h[b] * e->w[b], G0 = e->c0[b] / 32, Gt = G0 + e->L[b];
-        int8_t* store = e->arena[b % 2];                 // tile-major [tiles][Gt][128][32]
         for (int l = 0; l < e->L[b]; ++l) {
-            const dn8_engine::Layer& ly = e->layers[b][l];
-            dn8_conv1_args c1{};
-            c1.in0 = store; c1.seg = nullptr; c1.w = reinterpret_cast<const int8_t*>(ly.w1); c1.ab = ly.ab; c1.gd = ly.gd;
-            c1.out = e->bott; c1.err = e->err; c1.G0 = G0; c1.G = G0 + l; c1.N = cap; c1.HW = HW;
-            c1.prologue_f16 = e->c1_f16[b][l];
-            c1.tile_groups = Gt;
-            if ((ce = dn8::launch_conv1(c1, e->sms, st, true)) != cudaSuccess)
+            if ((ce = launch_conv1_of(e, b, l, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv1 b%d l%d: %s", b, l, cudaGetErrorString(ce));
             mark(e, DN8_K_CONV1, b, l, st);
-            dn8_conv2_args c2{};
-            c2.x = e->bott; c2.w = reinterpret_cast<const int8_t*>(ly.w2); c2.sc = ly.c2;
-            c2.out = store; c2.err = e->err;
-            c2.N = cap; c2.H = e->h[b]; c2.W = e->w[b];
-            c2.tile_groups = Gt; c2.group = G0 + l;
-            if ((ce = dn8::launch_conv2(e->c2plan[b], c2, e->sms, st, true)) != cudaSuccess)
+            if ((ce = launch_conv2_of(e, b, l, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "conv2 b%d l%d: %s", b, l, cudaGetErrorString(ce));
             mark(e, DN8_K_CONV2, b, l, st);
         }
+        if (b == last_block) break;
         if (e->trans[b]) {
-            dn8_trans_args t{};
-            t.in0 = store; t.seg = nullptr; t.w = reinterpret_cast<const int8_t*>(e->tw[b]); t.ab = e->tab[b]; t.gd = e->tgd[b];
-            t.out = e->arena[(b + 1) % 2]; t.err = e->err;
-            t.G0 = G0; t.G = Gt; t.N = cap; t.H = e->h[b]; t.W = e->w[b]; t.prologue_f16 = e->trans_f16[b];
-            t.tile_groups = Gt;
-            t.out_tile_groups = e->c0[b + 1] / 32 + e->L[b + 1];
-            if ((ce = dn8::launch_trans(t, e->sms, st, true)) != cudaSuccess)
+            if ((ce = launch_trans_of(e, b, st, true)) != cudaSuccess)
                 return efail(e, DN8_ECUDA, "transition %d: %s", b, cudaGetErrorString(ce));
             mark(e, DN8_K_TRANS, b, 0, st);
         } else {
             dn8_head_args hd{};
-            hd.in0 = store; hd.seg = nullptr; hd.fab = e->fab;
+            hd.in0 = e->arena[b % 2]; hd.seg = nullptr; hd.fab = e->fab;
             hd.tile_groups = Gt;
             const int C = Gt * 32;
             hd.feat = feat ? feat + static_cast<size_t>(img0) * C : nullptr;
@@ -352,6 +372,35 @@ static int engine_pass(dn8_engine* e, const dn8_input* in, int img0, int n, floa
         }
     }
     return DN8_OK;
+}
+
+int dn8_engine_forward_to(dn8_engine* e, const dn8_input* in, int32_t n, int32_t last_block, dn8_stream stream) {
+    if (e == nullptr || in == nullptr || in->x == nullptr || n < 1 || n > e->n || last_block < 0 ||
+        last_block >= e->n_blocks || (in->x_u8 && in->src == nullptr))
+        return efail(e, DN8_EINVAL, "forward_to: bad arguments (n must fit one pass, 0 <= last_block < %d)",
+                     e ? e->n_blocks : 0);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != e->device) cudaSetDevice(e->device);
+    const int rc = engine_pass(e, in, 0, n, nullptr, nullptr, nullptr, 0, static_cast<cudaStream_t>(stream), last_block);
+    if (prev != e->device) cudaSetDevice(prev);
+    return rc;
+}
+
+int dn8_engine_launch(dn8_engine* e, int32_t kind, int32_t block, int32_t layer, dn8_stream stream) {
+    if (e == nullptr || block < 0 || block >= e->n_blocks ||
+        !((kind == DN8_K_CONV1 || kind == DN8_K_CONV2) ? layer >= 0 && layer < e->L[block]
+                                                       : kind == DN8_K_TRANS && e->trans[block]))
+        return efail(e, DN8_EINVAL, "launch: no kernel of kind %d at block %d layer %d", kind, block, layer);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != e->device) cudaSetDevice(e->device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const cudaError_t ce = kind == DN8_K_CONV1 ? launch_conv1_of(e, block, layer, st, false)
+                         : kind == DN8_K_CONV2 ? launch_conv2_of(e, block, layer, st, false)
+                                               : launch_trans_of(e, block, st, false);
+    if (prev != e->device) cudaSetDevice(prev);
+    return ce == cudaSuccess ? DN8_OK : efail(e, DN8_ECUDA, "launch: %s", cudaGetErrorString(ce));
 }
 
 int dn8_engine_forward(dn8_engine* e, const dn8_input* in, int32_t n, float* feat, float* logits,

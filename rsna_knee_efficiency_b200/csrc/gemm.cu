@@ -74,6 +74,9 @@ struct GemmArgs {
     int sr;                   // raw ring slots
     int tg;                   // 0 = group-major planes; > 0 = tile-major input store with tg groups per tile
     int tg_out;               // transition: 0 = group-major output; > 0 = the next block's tile-major store
+    long long wait_limit;     // SM cycles a wait may take before the launch gives up (WAIT_LIMIT)
+    int fault;                // test hook (dn8_test_inject_wait_fault): 1 = the store producer of the first
+                              // CTA (pair) never posts raw stage 0 of its first tile, so a wait runs out
 };
 
 // Byte range [first, end) of the flattened input pixels (n * HW + y * W + x) a transition tile of
@@ -160,6 +163,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long lim = a.wait_limit;
     const int ntm = (rows + MT - 1) / MT;
     const int ntiles = ntm * a.nchunks;
     const int my_tiles = unit < ntiles ? (ntiles - 1 - unit) / nunits + 1 : 0;
@@ -239,27 +243,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
             bool ok_run = true;
             if (a.b_resident && T > 0) {
-                ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL);
-                if (PAIR && ok_run) ok_run = mbar_wait_w(&fullB[1], 0, a.err, s_abort, ERR_WAIT_FULL);   // the odd CTA's half
+                ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL, lim);
+                if (PAIR && ok_run) ok_run = mbar_wait_w(&fullB[1], 0, a.err, s_abort, ERR_WAIT_FULL, lim);   // the odd CTA's half
             }
             int i = 0;
             for (int t = 0; t < my_tiles && ok_run; ++t) {
                 const int acc = t & 1;
                 const int chunk = (unit + t * nunits) % a.nchunks;
                 const uint32_t idesc = idesc_u8s8(MT, min(NC, a.cout - chunk * NC));   // chunk width
-                if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+                if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC, lim)) break;
                 tc_fence_after();
                 for (int j = 0; j < NS; ++j, ++i) {
                     const int s = i % SA;
                     const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
-                    if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                    if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) { ok_run = false; break; }
                     uint32_t bbase;
                     int sbi = 0;
                     if (a.b_resident) {
                         bbase = b0 + j * KSTEP * btile;
                     } else {
                         sbi = i % a.sb;
-                        if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                        if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) { ok_run = false; break; }
                         bbase = b0 + sbi * bstage;
                     }
                     tc_fence_after();
@@ -334,12 +338,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 const int gc = min(KSTEP, G - j * KSTEP);
                 int ok = 1;
                 if (lane == 0) {
-                    ok = mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY) ? 1 : 0;
+                    ok = mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim) ? 1 : 0;
                     if (ok) mbar_expect_tx(&fullR[s], bytes * gc);
                 }
                 if (!__shfl_sync(0xffffffffu, ok, 0)) { ok_run = false; break; }
+                if (a.fault == 1 && blockIdx.x == 0 && i == 0) {
+                    // test hook: stage 0 is announced but never copied, so its consumers' wait runs out
+                    // (every other copy of the CTA is issued and lands long before that)
+                    continue;
+                }
                 if (TRANS && a.tg > 0) {
-                    // one 4 KB copy per tile of the span, tiles tg groups apart
+                    // one 4 KB copy per tile of the span, tiles tg groups apart (two groups per copy,
+                    // 8 KB contiguous, measured 19 % slower per transition on B200)
                     if (lane < ntl)
                         bulk_g2s(sR + s * RB + lane * 4096,
                                  a.in0 + off + (static_cast<size_t>(lane) * a.tg + j) * 4096, 4096u, &fullR[s]);
@@ -361,7 +371,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         if (lane == 0 && T > 0) {
             if (PAIR && rank == 1 && a.b_resident) {
                 // this CTA's weight half has landed: tell the issuing CTA
-                if (mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL)) mbar_arrive_at(&fullB[1], 0);
+                if (mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL, lim)) mbar_arrive_at(&fullB[1], 0);
             }
             if (!a.b_resident) {
                 int i = 0;
@@ -374,7 +384,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     for (int j = 0; j < NS; ++j, ++i) {
                         const int s = i % a.sb;
                         const int gc = min(KSTEP, G - j * KSTEP);
-                        if (!mbar_wait(&emptyB[s], ((i / a.sb) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
+                        if (!mbar_wait(&emptyB[s], ((i / a.sb) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) { ok_run = false; break; }
                         // the gc weight tiles of the stage are contiguous in the prepared table
                         mbar_expect_tx(&fullB[s], static_cast<uint32_t>(gc * cbt));
                         bulk_g2s(sB + s * bstage, wc + static_cast<size_t>(j) * KSTEP * cbt,
@@ -404,8 +414,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const int j_this = j;
             j += 2;
             while (j >= NS) j -= NS;
-            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
-            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+            // (the lanes of the warp poll the same barrier and abort flag in lockstep, so they leave
+            // together; tcgen05.st below is warp-collective)
+            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) break;
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) break;
             tc_fence_after();
             // res[16 h + 4 x + e]: unit x (K group), rows t/4 + 16 h (e < 2) and t/4 + 16 h + 8 (e >= 2),
             // K bytes 8 (t % 4) + 4 (e & 1) .. + 3; the registers stay live until tcgen05.wait::st
@@ -503,7 +515,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) off[jj] = x * 4096 + (jj * 32 + lane) * 16;
             }
-            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
+            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) break;
             uint4 q[8];
             if (active) {
 #pragma unroll
@@ -534,7 +546,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     }
                 }
             }
-            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) break;
             if (active) {
                 uint8_t* dst = sA + sa * ASTAGE + x * 4096;
 #pragma unroll
@@ -555,7 +567,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
         for (int t = 0; t < my_tiles; ++t) {
             const int acc = t & 1;
-            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC, lim)) break;
             tc_fence_after();
             const int tile = unit + t * nunits;
             const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
@@ -641,7 +653,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         if (threadIdx.x == 0) {
             for (int sl = 0; sl < SA && sl < T; ++sl) {
                 const int il = sl + SA * ((T - 1 - sl) / SA);          // last stage on barrier sl
-                if (!mbar_wait(&emptyA[sl], (il / SA) & 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+                if (!mbar_wait(&emptyA[sl], (il / SA) & 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) break;
             }
         }
         cluster_sync();
@@ -724,8 +736,23 @@ bool conv1_supported(int G) {
     return resident && smem <= 227 * 1024;
 }
 
+// dn8_test_inject_wait_fault: armed by the test hook, consumed by the next conv1 launch of the process.
+static std::atomic<int> g_fault_next{0};
+static std::atomic<long long> g_limit_next{0};
+
+void arm_wait_fault(int fault, long long wait_limit) {
+    g_limit_next.store(wait_limit, std::memory_order_relaxed);
+    g_fault_next.store(fault, std::memory_order_release);
+}
+
 cudaError_t launch_conv1(const dn8_conv1_args& a, int sms, cudaStream_t st, bool pdl) {
     GemmArgs g{};
+    g.wait_limit = WAIT_LIMIT;
+    if (const int f = g_fault_next.exchange(0, std::memory_order_acquire); f != 0) {
+        g.fault = f;
+        const long long lim = g_limit_next.load(std::memory_order_relaxed);
+        g.wait_limit = lim > 0 ? lim : WAIT_LIMIT;
+    }
     g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
     g.out = a.out; g.err = a.err;
     g.G0 = a.G0; g.G = a.G; g.N = a.N; g.HW = a.HW; g.W = 0;
@@ -742,12 +769,12 @@ int trans_chunk(int cout) { return cout >= 256 ? 256 : 128; }
 // Largest raw span of a transition tile: its 128 consecutive pooled pixels cover at most
 // 128 / W2 pooled rows when W2 divides 128 (tiles start on a row), else ceil(128 / W2) + 1;
 // each pooled row needs two whole input rows.
+// tiled: whole 4 KB tiles; a span of 2 prow W pixels starting anywhere covers at most span / 128 + 2
+// of them, exactly span / 128 when it starts on a tile (W / 2 divides 128: every block at 512 px).
 static int trans_raw_bytes(int W, bool tiled) {
     const int W2 = W / 2;
     const int prow = (128 % W2 == 0) ? 128 / W2 : (128 + W2 - 1) / W2 + 1;
     if (tiled) {
-        // whole 4 KB tiles: a span of 2 prow W pixels starting anywhere covers at most this many,
-        // exactly 2 prow W / 128 when the span starts on a tile (W / 2 divides 128: every block at 512 px)
         const int span = 2 * prow * W;
         return (128 % W2 == 0 && span % 128 == 0 ? span / 128 : span / 128 + 2) * 4096;
     }
@@ -756,6 +783,7 @@ static int trans_raw_bytes(int W, bool tiled) {
 
 cudaError_t launch_trans(const dn8_trans_args& a, int sms, cudaStream_t st, bool pdl) {
     GemmArgs g{};
+    g.wait_limit = WAIT_LIMIT;
     const int cout = a.G * 16;
     g.in0 = a.in0; g.seg = a.seg; g.wu = reinterpret_cast<const uint8_t*>(a.w); g.ab = a.ab; g.gd = a.gd;
     g.out = a.out; g.err = a.err;

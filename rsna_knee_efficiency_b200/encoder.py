@@ -6,8 +6,10 @@ same call contract: `enc(x)` with x (N, 3, img, img) fp16/float on cuda:dev retu
 encoder's own buffer `out[:N]` (N, n_features) float32, valid until the next call; the work runs
 on a private stream that waits on the caller's stream, and the caller's stream waits on it before
 returning. `capture(n)` records CUDA graphs, `graph_in_buf(n)` exposes the static input buffer the
-reference's inference loop fills in place, `store(b, j)` decodes a store segment. Errors: a bad
-pack or geometry raises ValueError (as the reference), CUDA failures RuntimeError.
+reference's inference loop fills in place; the diagnostics `store(b, j)` (one store segment),
+`trace(x)` (every block's store and the features), `profile` (device ms of every launch of a pass)
+and `time_layers(reps)` (every conv1 / conv2 / transition timed alone) are the reference's. Errors:
+a bad pack or geometry raises ValueError (as the reference), CUDA failures RuntimeError.
 
 Beyond the reference: `encode_u8` feeds the uint8 volume planes straight into the stem (gather +
 normalise + optional horizontal flip fused) and returns the head's logits and per-view means.
@@ -241,6 +243,77 @@ class Dense8SEncoder:
         self.stream.synchronize()
         t = buf.view(groups, self.nb, hw, 32).permute(1, 0, 3, 2).reshape(self.nb, groups * 32, b["h"], b["w"])
         return t.float()
+
+    @torch.no_grad()
+    def trace(self, x: torch.Tensor) -> tuple[dict, torch.Tensor]:
+        """One pass over the first `nb` images of x (N, 3, img, img) with every block's store: returns
+        ({(block, j): float (nb, c, h, w)}, features (nb, n_features)) like the reference's `trace`
+        (src/knee/dense8s.py:1509-1546; j = 0 the block input, j >= 1 the output of layer j - 1). The
+        blocks alternate between two arenas, so the stores are read after partial passes that stop
+        after blocks 1, 3, ... (passes are deterministic) and the features from a full pass."""
+        xh = x[:self.nb].to(self.in_dtype).contiguous()
+        n = xh.shape[0]
+        f = torch.zeros((self.nb, self.n_features), dtype=torch.float32, device=f"cuda:{self.dev}")
+        inp = nat.Input(xh.data_ptr(), None, None, 0)
+        blocks = self.meta["blocks"]
+        out: dict = {}
+        self.stream.wait_stream(torch.cuda.current_stream(self.dev))
+        for last in range(len(blocks)):
+            if last % 2 == 0 and last != len(blocks) - 1:
+                continue
+            nat.check(nat.lib().dn8_engine_forward_to(self._h, ctypes.byref(inp), n, last, self.stream.cuda_stream),
+                      "dn8_engine_forward_to", self._h)
+            for bi in (last - 1, last):                  # store() synchronises the encoder's stream
+                if bi >= 0 and (bi, 0) not in out:
+                    for j in range(blocks[bi]["L"] + 1):
+                        out[(bi, j)] = self.store(bi, j)[:n]
+        with torch.cuda.stream(self.stream):
+            self._forward(inp, n, f.data_ptr())
+        self.stream.synchronize()
+        self.check()
+        return out, f[:n]
+
+    def _time(self, fn, reps: int = 20) -> float:
+        """ms per call of `fn` (launches on the encoder's stream): a CUDA graph of `reps` calls,
+        replayed once as warm-up and once under events (the reference's `_time`,
+        src/knee/dense8s.py:1565-1581)."""
+        with torch.cuda.device(self.dev), torch.cuda.stream(self.stream):
+            fn()
+            self.stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream, capture_error_mode="thread_local"):
+                for _ in range(reps):
+                    fn()
+            g.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            g.replay()
+            e1.record(self.stream)
+            self.stream.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def time_layers(self, reps: int = 20) -> dict:
+        """ms of every conv1, conv2 and transition of a pass, each launched `reps` times back to back
+        on the current store (the reference's `time_layers`, src/knee/dense8s.py:1583-1596): keys
+        "c1 b{block}l{layer}", "c2 b{block}l{layer}", "t{block}"."""
+        out: dict = {}
+        lib = nat.lib()
+
+        def launcher(kind, b, l):
+            def fn():
+                nat.check(lib.dn8_engine_launch(self._h, kind, b, l, self.stream.cuda_stream),
+                          "dn8_engine_launch", self._h)
+            return fn
+
+        for bi, b in enumerate(self.meta["blocks"]):
+            for li in range(b["L"]):
+                out[f"c1 b{bi}l{li}"] = round(self._time(launcher(nat.K_CONV1, bi, li), reps), 4)
+                out[f"c2 b{bi}l{li}"] = round(self._time(launcher(nat.K_CONV2, bi, li), reps), 4)
+            if b["trans"]:
+                out[f"t{bi}"] = round(self._time(launcher(nat.K_TRANS, bi, 0), reps), 4)
+        self.check()
+        return out
 
     def profile(self, x: torch.Tensor | None = None, planes=None, src=None, flags=None,
                 reps: int = 3) -> list:

@@ -151,3 +151,25 @@ def test_logits_512_within_1e3_of_reference_emulate_fixture():
     err = float(np.abs(views.cpu().numpy()[0] - want.mean(0)).max())
     print(f"512 px vs the reference's emulate(): view-mean logits {err:.2e}, per-image logits {per_image:.2e}")
     assert err <= 1e-3
+
+
+def test_trace_matches_oracle_stores_and_time_layers_runs():
+    """`trace` (the reference's per-block store dump) gives the oracle's store of every block and
+    layer and its features; `time_layers` times every conv1 / conv2 / transition of a pass (keys as
+    the reference's) and leaves the engine usable (a later call still gives the oracle's bytes)."""
+    _, plan, par = plan_tables(64)
+    n = 3
+    x = synth.triplets(synth.volume(12, H=64, W=64))[:n]
+    enc = _encoder(plan, n)
+    stores, feats = enc.trace(_x16(x))
+    tr = {}
+    want = orc.forward(par, packmod.pack_meta(plan, n), x, mode=orc.KERNEL, trace=tr)
+    np.testing.assert_array_equal(feats.cpu().numpy(), want)
+    assert set(stores) == set(tr)
+    for key, t in tr.items():
+        np.testing.assert_array_equal(stores[key].cpu().numpy().astype(np.int8), t, err_msg=str(key))
+    times = enc.time_layers(reps=3)
+    blocks = enc.meta["blocks"]
+    assert len(times) == sum(2 * b["L"] for b in blocks) + sum(1 for b in blocks if b["trans"])
+    assert all(v > 0 for v in times.values()) and "c1 b3l31" in times and "t2" in times
+    np.testing.assert_array_equal(enc(_x16(x)).cpu().numpy(), want)
