@@ -138,7 +138,8 @@ int dn8_stem(const dn8_stem_args* a, dn8_stream stream);
  * src/knee/dense8s.py:1379-1385) and adds the benchmark head (linear C -> n_out, mean over the
  * slices of a view). features = mean over pixels of relu(a_c q + b_c) (F_ab, the reference's
  * summation order); logits = features . Hw^T + Hb (fp32); view_logits[v] = mean of the logits of
- * images v*per_view .. v*per_view + per_view - 1. One CTA per image. */
+ * images v*per_view .. v*per_view + per_view - 1. A cluster of four CTAs per image; G <= 72
+ * (2304 channels), n_out <= 64. */
 typedef struct dn8_head_args {
     const int8_t* in0;      /* last block's input groups, group-major [G0][N][HW][32] */
     const int8_t* seg;      /* its layer segments [L][N][HW][32] */

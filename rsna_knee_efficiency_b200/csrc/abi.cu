@@ -167,9 +167,9 @@ int dn8_stem(const dn8_stem_args* a, dn8_stream stream) {
 
 int dn8_head(const dn8_head_args* a, dn8_stream stream) {
     if (a == nullptr) return fail(DN8_EINVAL, "dn8_head: null arguments");
-    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64 ||
-        a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G))
-        return fail(DN8_EINVAL, "dn8_head: bad geometry");
+    if (a->G < 1 || a->G > 72 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 ||
+        a->n_out > 64 || a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G))
+        return fail(DN8_EINVAL, "dn8_head: bad geometry (G <= 72, n_out <= 64)");
     if (!aligned16(a->in0) || (a->tile_groups == 0 && !aligned16(a->seg)) || a->fab == nullptr)
         return fail(DN8_EINVAL, "dn8_head: bad pointers");
     if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))
@@ -202,9 +202,9 @@ int dn8_head_noalloc(const dn8_head_args* a, dn8_stream stream) {
                     a->N / a->per_view, DN8_HEAD_SCRATCH_VIEWS);
     if (a->tickets != nullptr)
         return fail(DN8_EINVAL, "dn8_head_noalloc: tickets must be NULL (the built-in scratch is used)");
-    if (a->G < 1 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 || a->n_out > 64 ||
-        a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G))
-        return fail(DN8_EINVAL, "dn8_head_noalloc: bad geometry");
+    if (a->G < 1 || a->G > 72 || a->G0 < 1 || a->G0 > a->G || a->N < 1 || a->HW < 1 || a->n_out < 0 ||
+        a->n_out > 64 || a->tile_groups < 0 || (a->tile_groups > 0 && a->tile_groups < a->G))
+        return fail(DN8_EINVAL, "dn8_head_noalloc: bad geometry (G <= 72, n_out <= 64)");
     if (!aligned16(a->in0) || (a->tile_groups == 0 && !aligned16(a->seg)) || a->fab == nullptr)
         return fail(DN8_EINVAL, "dn8_head_noalloc: bad pointers");
     if (a->hw != nullptr && (a->hb == nullptr || a->logits == nullptr))

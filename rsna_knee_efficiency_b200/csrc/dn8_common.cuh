@@ -184,6 +184,15 @@ DN8_DEV void mbar_arrive_at(uint64_t* bar, uint32_t rank) {
                  "mbarrier.arrive.shared::cluster.b64 _, [ra];\n\t}"
                  ::"r"(smem_u32(bar)), "r"(rank) : "memory");
 }
+// A float of CTA `rank`'s shared memory at the offset of `p` in this CTA (distributed shared memory).
+DN8_DEV float ld_peer_f32(const float* p, uint32_t rank) {
+    float v;
+    asm volatile("{\n\t.reg .b32 ra;\n\t"
+                 "mapa.shared::cluster.u32 ra, %1, %2;\n\t"
+                 "ld.shared::cluster.f32 %0, [ra];\n\t}"
+                 : "=f"(v) : "r"(smem_u32(p)), "r"(rank) : "memory");
+    return v;
+}
 // One full warp of EACH CTA of the pair (the same warp) allocates; both get the same base address.
 DN8_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"

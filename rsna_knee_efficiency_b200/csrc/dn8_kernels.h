@@ -26,10 +26,10 @@ cudaError_t launch_pdl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
 }
 
-// As launch_pdl, as clusters of two CTAs (grid.x even).
+// As launch_pdl, as clusters of `csize` CTAs along x (grid.x a multiple of csize).
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl_pairs(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                             Args&&... args) {
+cudaError_t launch_pdl_cluster(bool pdl, int csize, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t st, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -37,7 +37,7 @@ cudaError_t launch_pdl_pairs(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -45,6 +45,13 @@ cudaError_t launch_pdl_pairs(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
+// As launch_pdl, as clusters of two CTAs (grid.x even).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_pairs(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args&&... args) {
+    return launch_pdl_cluster(pdl, 2, kernel, grid, block, smem, st, static_cast<Args&&>(args)...);
 }
 
 __attribute__((visibility("hidden"))) void set_last_error(const char* msg);  // thread-local message (abi.cu)

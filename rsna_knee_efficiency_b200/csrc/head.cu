@@ -1,5 +1,6 @@
 // head.cu -- global pooling of the last block (norm5 with sigma folded, ReLU, spatial mean) and the
-// linear head in one reduction kernel: one CTA per image.
+// linear head in one reduction kernel: a cluster of four CTAs per image, each pooling a quarter of
+// the channel groups; the first CTA gathers the features over distributed shared memory.
 //   features f[n][c] = (p0 + p1 + p2 + p3) / HW with p_q the fp32 sum, in ascending pixel order, of
 //     relu(fmaf(a_c, q, b_c)) over pixels s = q, q + 4, ...: the reference's `final_q`
 //     (src/knee/dense8s_kernels.cu:2306-2323), bit for bit;
@@ -13,21 +14,29 @@
 
 namespace dn8 {
 
-constexpr int HD_THREADS = 512;
+constexpr int HD_THREADS = 128;
+constexpr int HD_CLUSTER = 4;              // CTAs per image: each pools a quarter of the groups
+constexpr int HD_MAX_SLICE = 18;           // groups of a quarter (G <= 72, the 2304 channels dn8_head takes)
 
+// Image n = blockIdx.x / HD_CLUSTER; CTA r of its cluster pools groups [r G / 4, (r + 1) G / 4).
+// task = (group, 16-channel half, partial q): one 16-byte load per pixel feeds 16 channel sums; each
+// channel's partial q is summed in ascending pixel order.
 __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args a) {
     extern __shared__ float hs[];
-    const int C = a.G * 32, HW = a.HW, n = blockIdx.x;
+    const int C = a.G * 32, HW = a.HW;
+    const int n = blockIdx.x / HD_CLUSTER;
+    const uint32_t rank = cluster_rank();
+    const int g0 = static_cast<int>(rank) * a.G / HD_CLUSTER, g1 = (static_cast<int>(rank) + 1) * a.G / HD_CLUSTER;
     const size_t nal = static_cast<size_t>(a.n_alloc > a.N ? a.n_alloc : a.N);
-    float* part = hs;                          // [4][C]
-    float* feat = hs + 4 * C;                  // [C]
+    float* part = hs;                          // [4][HD_MAX_SLICE * 32]: this CTA's channels
+    float* feat = hs + 4 * HD_MAX_SLICE * 32;  // [C] (this CTA's channels; rank 0 gathers all of them)
     float* red = feat + C;                     // [HD_THREADS / 32][NOUT]
     const int tid = threadIdx.x;
     griddep_launch_dependents();
     griddep_wait();                            // the last block's store
-    // task = (group g, half h, partial q): 16 channels, pixels q, q + 4, ...
-    for (int task = tid; task < a.G * 8; task += HD_THREADS) {
-        const int g = task >> 3, h = (task >> 2) & 1, q = task & 3;
+    constexpr int SL = HD_MAX_SLICE * 32;
+    for (int task = tid; task < (g1 - g0) * 8; task += HD_THREADS) {
+        const int g = g0 + (task >> 3), h = (task >> 2) & 1, q = task & 3;        // channels 16 h .. 16 h + 15
         // pixel s of image n in group g: group-major planes, or the tile-major store (pixel p = n HW + s
         // at tile p / 128, row p % 128)
         const int8_t* base;
@@ -44,14 +53,14 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
         float av[16], bv[16], acc[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-            const float2 p = ab[k];
-            av[k] = p.x;
-            bv[k] = p.y;
+            const float2 pr = ab[k];
+            av[k] = pr.x;
+            bv[k] = pr.y;
             acc[k] = 0.0f;
         }
-        // (unrolled so that several pixels' loads are in flight; each channel's sum still runs in
-        // ascending pixel order)
-#pragma unroll 4
+        // (unrolled so that 16 pixels' loads are in flight: the chain of a thread is HW / 4 pixels long;
+        // each channel's sum still runs in ascending pixel order)
+#pragma unroll 16
         for (int s = q; s < HW; s += 4) {
             const size_t p = p0 + s;
             const int8_t* src = a.tile_groups > 0 ? base + (p >> 7) * tstride + (p & 127) * 32 : base + p * 32;
@@ -65,30 +74,40 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
             }
         }
 #pragma unroll
-        for (int k = 0; k < 16; ++k) part[q * C + g * 32 + h * 16 + k] = acc[k];
+        for (int k = 0; k < 16; ++k) part[q * SL + (g - g0) * 32 + h * 16 + k] = acc[k];
     }
     __syncthreads();
-    for (int c = tid; c < C; c += HD_THREADS) {
-        const float f = (part[c] + part[C + c] + part[2 * C + c] + part[3 * C + c]) / static_cast<float>(HW);
+    for (int c = g0 * 32 + tid; c < g1 * 32; c += HD_THREADS) {
+        const int cl = c - g0 * 32;
+        const float f = (part[cl] + part[SL + cl] + part[2 * SL + cl] + part[3 * SL + cl]) / static_cast<float>(HW);
         feat[c] = f;
         if (a.feat != nullptr) a.feat[static_cast<size_t>(n) * C + c] = f;
     }
+    cluster_sync();                            // every CTA's features are in its shared memory
+    if (rank == 0 && a.hw != nullptr) {
+        // gather the other CTAs' channels (distributed shared memory)
+        for (uint32_t r = 1; r < HD_CLUSTER; ++r) {
+            const int c0 = static_cast<int>(r) * a.G / HD_CLUSTER * 32, c1 = (static_cast<int>(r) + 1) * a.G / HD_CLUSTER * 32;
+            for (int c = c0 + tid; c < c1; c += HD_THREADS) feat[c] = ld_peer_f32(&feat[c], r);
+        }
+    }
+    cluster_sync();                            // the peers' shared memory stays until rank 0 has read it
+    if (rank != 0 || a.hw == nullptr) return;
     __syncthreads();
-    if (a.hw == nullptr) return;
     // logits: each warp reduces a strided share of the channels for every output, then a fixed tree
     const int warp = tid >> 5, lane = tid & 31, nw = HD_THREADS / 32;
     for (int j = 0; j < a.n_out; ++j) {
-        float s = 0.0f;
-        for (int c = tid; c < C; c += HD_THREADS) s = fmaf(feat[c], a.hw[static_cast<size_t>(j) * C + c], s);
+        float sm = 0.0f;
+        for (int c = tid; c < C; c += HD_THREADS) sm = fmaf(feat[c], a.hw[static_cast<size_t>(j) * C + c], sm);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) red[warp * a.n_out + j] = s;
+        for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        if (lane == 0) red[warp * a.n_out + j] = sm;
     }
     __syncthreads();
     if (tid < a.n_out) {
-        float s = 0.0f;
-        for (int w = 0; w < nw; ++w) s += red[w * a.n_out + tid];
-        a.logits[static_cast<size_t>(n) * a.n_out + tid] = s + a.hb[tid];
+        float sm = 0.0f;
+        for (int w = 0; w < nw; ++w) sm += red[w * a.n_out + tid];
+        a.logits[static_cast<size_t>(n) * a.n_out + tid] = sm + a.hb[tid];
     }
     if (a.view_logits == nullptr || a.per_view < 1) return;
     // the last image of a view to finish averages the view's logits in image order
@@ -104,10 +123,10 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
     if (s_last) {
         __threadfence();
         if (tid < a.n_out) {
-            float s = 0.0f;
+            float sm = 0.0f;
             for (int k = 0; k < a.per_view; ++k)
-                s += __ldcg(a.logits + static_cast<size_t>(v * a.per_view + k) * a.n_out + tid);
-            a.view_logits[static_cast<size_t>(v) * a.n_out + tid] = s / static_cast<float>(a.per_view);
+                sm += __ldcg(a.logits + static_cast<size_t>(v * a.per_view + k) * a.n_out + tid);
+            a.view_logits[static_cast<size_t>(v) * a.n_out + tid] = sm / static_cast<float>(a.per_view);
         }
         if (tid == 0) a.tickets[v] = 0;
     }
@@ -142,11 +161,12 @@ cudaError_t head_scratch_tickets(int32_t** out) {
 
 cudaError_t launch_head(const dn8_head_args& a, cudaStream_t st, bool pdl) {
     const int C = a.G * 32;
-    const size_t smem = (static_cast<size_t>(5) * C + (HD_THREADS / 32) * (a.n_out > 0 ? a.n_out : 1)) * sizeof(float);
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    const size_t smem =
+        (static_cast<size_t>(4) * HD_MAX_SLICE * 32 + C + (HD_THREADS / 32) * (a.n_out > 0 ? a.n_out : 1)) * sizeof(float);
+    if (a.G > HD_CLUSTER * HD_MAX_SLICE) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    return launch_pdl(pdl, head_kernel, dim3(a.N), dim3(HD_THREADS), smem, st, a);
+    return launch_pdl_cluster(pdl, HD_CLUSTER, head_kernel, dim3(a.N * HD_CLUSTER), dim3(HD_THREADS), smem, st, a);
 }
 
 }  // namespace dn8

@@ -173,3 +173,19 @@ def test_trace_matches_oracle_stores_and_time_layers_runs():
     assert len(times) == sum(2 * b["L"] for b in blocks) + sum(1 for b in blocks if b["trans"])
     assert all(v > 0 for v in times.values()) and "c1 b3l31" in times and "t2" in times
     np.testing.assert_array_equal(enc(_x16(x)).cpu().numpy(), want)
+
+
+def test_reference_written_pack_runs_bit_exact():
+    """A pack written by the reference's own save_pack (tests/golden/ref_pack_64.npz: a 6 / 4 / 1-layer
+    DenseNet at 64 px, fp16 prologues in block 1 and transition 1, fp32 elsewhere) loads into the
+    engine and gives the oracle's features on the pack's own tables and kernel choices."""
+    from pathlib import Path
+    pk = packmod.load_pack(Path(__file__).resolve().parent / "golden" / "ref_pack_64.npz")
+    n = pk["meta"]["n"]
+    x = synth.triplets(synth.volume(31, H=64, W=64))[:n]
+    enc = Dense8SEncoder(pk, 0, n)
+    got = enc(_x16(x)).cpu().numpy()
+    enc.check()
+    assert got.shape == (n, pk["meta"]["n_features"])
+    np.testing.assert_array_equal(got, orc.forward(pk["par"], pk["meta"], x, mode=orc.KERNEL))
+    enc.close()

@@ -242,3 +242,26 @@ def test_plane_table_addresses_the_seed_windows(flip):
                     assert src[i, :3].tolist() == [(s * studies + st) * slices + p + d for d in range(3)]
                     assert flags[i] == f
                     i += 1
+
+
+def test_reference_written_pack_loads():
+    """tests/golden/ref_pack_64.npz was written by the reference's own save_pack (conv2 "ours",
+    stem "i8"): load_pack reads its meta and tables, the fp16 / fp32 prologue choice per layer follows
+    the reference's kernel kinds, and every table the engine needs is there with its dtype and size."""
+    from pathlib import Path
+    pk = packmod.load_pack(Path(__file__).resolve().parent / "golden" / "ref_pack_64.npz")
+    meta, par = pk["meta"], pk["par"]
+    assert packmod.is_pack(pk) and meta["conv2"] == "ours" and meta["stem"] == "i8" and meta["n"] == 2
+    assert packmod.f16_layers(meta) == {(0, li) for li in range(6)} | {("t", 0)}
+    for bi, b in enumerate(meta["blocks"]):
+        for li in range(b["L"]):
+            cin = b["c0"] + 32 * li
+            assert par[f"L{bi}_{li}_w1"].shape == (cin // 32, 128, 32) and par[f"L{bi}_{li}_w1"].dtype == np.int8
+            assert par[f"L{bi}_{li}_w2k"].shape == (4, 9, 32, 32)
+            assert par[f"L{bi}_{li}_abh"].shape == (cin // 2, 4) and par[f"L{bi}_{li}_ab"].shape == (cin, 2)
+            assert par[f"L{bi}_{li}_gdu"].dtype == np.float32 and par[f"L{bi}_{li}_c2u"].shape == (32,)
+        if b["trans"]:
+            ctot = b["c0"] + 32 * b["L"]
+            assert par[f"T{bi}_w"].shape == (ctot // 32, ctot // 2, 32)
+    assert par["S_w8"].shape == (64, 176) and par["S_kc"].shape == (128,)
+    assert par["F_ab"].shape == (meta["n_features"], 2)
