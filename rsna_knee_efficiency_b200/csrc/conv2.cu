@@ -109,7 +109,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         if (lane == 0 && my_tiles > 0) {
             for (int t = 0; t < my_tiles; ++t) {
                 const int s = t % C2_STAGES;
-                if (!mbar_wait(&empty[s], ((t / C2_STAGES) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) break;
+                if (!mbar_wait(&empty[s], ((t / C2_STAGES) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (33 << 4))) break;
                 const int tile = blockIdx.x + t * gridDim.x;
                 const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
                 mbar_expect_tx(&full[s], 8u * PL);
@@ -121,12 +121,12 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         // ---------------- MMA issuer (the whole warp; one elected lane issues) ----------------
         const uint32_t idesc = idesc_u8s8(128, 96);
         const uint32_t x0 = smem_u32(sX), w0 = smem_u32(sW);
-        const bool wok = my_tiles == 0 || mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+        const bool wok = my_tiles == 0 || mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL | (34 << 4));
         for (int t = 0; t < my_tiles && wok; ++t) {
             const int acc = t & 1, s = t % C2_STAGES;
-            if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) break;
+            if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC | (35 << 4))) break;
             tc_fence_after();
-            if (!mbar_wait_w(&full[s], (t / C2_STAGES) & 1, a.err, s_abort, ERR_WAIT_FULL)) break;
+            if (!mbar_wait_w(&full[s], (t / C2_STAGES) & 1, a.err, s_abort, ERR_WAIT_FULL | (36 << 4))) break;
             tc_fence_after();
             const uint32_t xs = x0 + s * stage_bytes;
 #pragma unroll
@@ -158,7 +158,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
 
         auto load = [&](int t, uint32_t (&d0)[16], uint32_t (&d1)[16], uint32_t (&d2)[16]) -> bool {
             const int acc = t & 1;
-            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) return false;
+            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (37 << 4))) return false;
             tc_fence_after();
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * 128 + ch * 16;
             tmem_ld16(taddr, d0);
@@ -189,7 +189,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             if (lane == 0) mbar_arrive(&xbar[(t % C2_XBUF) * 2 + ch]);
         };
         auto wait_x = [&](int t) -> bool {
-            return mbar_wait(&xbar[(t % C2_XBUF) * 2 + ch], (t / C2_XBUF) & 1, a.err, s_abort, ERR_WAIT_ACC);
+            return mbar_wait(&xbar[(t % C2_XBUF) * 2 + ch], (t / C2_XBUF) & 1, a.err, s_abort, ERR_WAIT_ACC | (38 << 4));
         };
         // out[p] = D[p-1][0] + D[p][1] + D[p+1][2] (zero outside the row). The in-warp neighbours are
         // added right after the load (so 16 sums, not 48 taps, stay live across the exchange);

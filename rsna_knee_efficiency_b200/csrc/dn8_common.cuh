@@ -23,6 +23,8 @@ enum : int {
     ERR_WAIT_ACC = 3,       // MMA / epilogue accumulator hand-off
     ERR_SHAPE = 4,          // launch arguments outside what the kernel supports
 };
+// A kernel may add the wait site in bits 4-11 (code = kind | site << 4), so that a device error
+// names the barrier that ran out.
 // ~2^32 SM cycles (about 2 s at 2 GHz): far beyond any legitimate wait of these kernels.
 constexpr long long WAIT_LIMIT = 1ll << 32;
 

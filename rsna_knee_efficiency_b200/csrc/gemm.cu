@@ -243,27 +243,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
             bool ok_run = true;
             if (a.b_resident && T > 0) {
-                ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL, lim);
-                if (PAIR && ok_run) ok_run = mbar_wait_w(&fullB[1], 0, a.err, s_abort, ERR_WAIT_FULL, lim);   // the odd CTA's half
+                ok_run = mbar_wait_w(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL | (1 << 4), lim);
+                if (PAIR && ok_run) ok_run = mbar_wait_w(&fullB[1], 0, a.err, s_abort, ERR_WAIT_FULL | (2 << 4), lim);   // the odd CTA's half
             }
             int i = 0;
             for (int t = 0; t < my_tiles && ok_run; ++t) {
                 const int acc = t & 1;
                 const int chunk = (unit + t * nunits) % a.nchunks;
                 const uint32_t idesc = idesc_u8s8(MT, min(NC, a.cout - chunk * NC));   // chunk width
-                if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC, lim)) break;
+                if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC | (3 << 4), lim)) break;
                 tc_fence_after();
                 for (int j = 0; j < NS; ++j, ++i) {
                     const int s = i % SA;
                     const int gc = min(KSTEP, G - j * KSTEP);        // K groups in this stage
-                    if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) { ok_run = false; break; }
+                    if (!mbar_wait_w(&fullA[s], (i / SA) & 1, a.err, s_abort, ERR_WAIT_FULL | (4 << 4), lim)) { ok_run = false; break; }
                     uint32_t bbase;
                     int sbi = 0;
                     if (a.b_resident) {
                         bbase = b0 + j * KSTEP * btile;
                     } else {
                         sbi = i % a.sb;
-                        if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) { ok_run = false; break; }
+                        if (!mbar_wait_w(&fullB[sbi], (i / a.sb) & 1, a.err, s_abort, ERR_WAIT_FULL | (5 << 4), lim)) { ok_run = false; break; }
                         bbase = b0 + sbi * bstage;
                     }
                     tc_fence_after();
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 const int gc = min(KSTEP, G - j * KSTEP);
                 int ok = 1;
                 if (lane == 0) {
-                    ok = mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim) ? 1 : 0;
+                    ok = mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (6 << 4), lim) ? 1 : 0;
                     if (ok) mbar_expect_tx(&fullR[s], bytes * gc);
                 }
                 if (!__shfl_sync(0xffffffffu, ok, 0)) { ok_run = false; break; }
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         if (lane == 0 && T > 0) {
             if (PAIR && rank == 1 && a.b_resident) {
                 // this CTA's weight half has landed: tell the issuing CTA
-                if (mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL, lim)) mbar_arrive_at(&fullB[1], 0);
+                if (mbar_wait(&fullB[0], 0, a.err, s_abort, ERR_WAIT_FULL | (7 << 4), lim)) mbar_arrive_at(&fullB[1], 0);
             }
             if (!a.b_resident) {
                 int i = 0;
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     for (int j = 0; j < NS; ++j, ++i) {
                         const int s = i % a.sb;
                         const int gc = min(KSTEP, G - j * KSTEP);
-                        if (!mbar_wait(&emptyB[s], ((i / a.sb) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) { ok_run = false; break; }
+                        if (!mbar_wait(&emptyB[s], ((i / a.sb) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (8 << 4), lim)) { ok_run = false; break; }
                         // the gc weight tiles of the stage are contiguous in the prepared table
                         mbar_expect_tx(&fullB[s], static_cast<uint32_t>(gc * cbt));
                         bulk_g2s(sB + s * bstage, wc + static_cast<size_t>(j) * KSTEP * cbt,
@@ -416,8 +416,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             while (j >= NS) j -= NS;
             // (the lanes of the warp poll the same barrier and abort flag in lockstep, so they leave
             // together; tcgen05.st below is warp-collective)
-            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) break;
-            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) break;
+            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL | (9 << 4), lim)) break;
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (10 << 4), lim)) break;
             tc_fence_after();
             // res[16 h + 4 x + e]: unit x (K group), rows t/4 + 16 h (e < 2) and t/4 + 16 h + 8 (e >= 2),
             // K bytes 8 (t % 4) + 4 (e & 1) .. + 3; the registers stay live until tcgen05.wait::st
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) off[jj] = x * 4096 + (jj * 32 + lane) * 16;
             }
-            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL, lim)) break;
+            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL | (11 << 4), lim)) break;
             uint4 q[8];
             if (active) {
 #pragma unroll
@@ -546,7 +546,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     }
                 }
             }
-            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) break;
+            if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (12 << 4), lim)) break;
             if (active) {
                 uint8_t* dst = sA + sa * ASTAGE + x * 4096;
 #pragma unroll
@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
         for (int t = 0; t < my_tiles; ++t) {
             const int acc = t & 1;
-            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC, lim)) break;
+            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (13 << 4), lim)) break;
             tc_fence_after();
             const int tile = unit + t * nunits;
             const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
@@ -653,7 +653,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         if (threadIdx.x == 0) {
             for (int sl = 0; sl < SA && sl < T; ++sl) {
                 const int il = sl + SA * ((T - 1 - sl) / SA);          // last stage on barrier sl
-                if (!mbar_wait(&emptyA[sl], (il / SA) & 1, a.err, s_abort, ERR_WAIT_EMPTY, lim)) break;
+                if (!mbar_wait(&emptyA[sl], (il / SA) & 1, a.err, s_abort, ERR_WAIT_EMPTY | (14 << 4), lim)) break;
             }
         }
         cluster_sync();

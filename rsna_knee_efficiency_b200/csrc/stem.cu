@@ -145,7 +145,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 bulk_g2s(sW, a.w, ST_WBYTES, &wfull[0]);
             }
             __syncwarp();
-            bool ok_run = mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL);
+            bool ok_run = mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL | (65 << 4));
             const uint32_t idesc = idesc_u8s8(128, 64);
             const uint32_t a0 = smem_u32(sRec), w0 = smem_u32(sW);
             int i = 0;
@@ -154,8 +154,8 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 task_rows(t, n, py0, cr0, nrows);
                 for (int r = 0; r < nrows; ++r, ++i) {
                     const int b = i & 1, cr = cr0 + r;
-                    if (!mbar_wait_w(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
-                    if (!mbar_wait_w(&fullA[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                    if (!mbar_wait_w(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC | (66 << 4))) { ok_run = false; break; }
+                    if (!mbar_wait_w(&fullA[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL | (67 << 4))) { ok_run = false; break; }
                     tc_fence_after();
                     for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -225,7 +225,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 if (r == 0) {
                     // a new band reuses ring slots the previous conv row may still be reading: wait
                     // until every producer warp has finished that row's im2col tile
-                    if (i > 0 && !mbar_wait(&fullA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) {
+                    if (i > 0 && !mbar_wait(&fullA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL | (68 << 4))) {
                         ok_run = false;
                         break;
                     }
@@ -241,7 +241,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ringrdy[i & 1]);
-                if (!mbar_wait(&ringrdy[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL)) { ok_run = false; break; }
+                if (!mbar_wait(&ringrdy[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL | (69 << 4))) { ok_run = false; break; }
                 // the next conv row's input rows load while this row's im2col tile is built
                 if (r + 1 < nrows) {
                     fetch(n, 2 * cr + 4, pre0);
@@ -250,9 +250,9 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 const int b = i & 1;
                 // the new records overwrite the slots last read by conv row i - 2 (and, at a band's
                 // first row, by conv row i - 1 too): wait until the MMAs of those rows are done
-                if (!mbar_wait(&emptyA[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
+                if (!mbar_wait(&emptyA[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (70 << 4))) { ok_run = false; break; }
                 if (r == 0 && i > 0 &&
-                    !mbar_wait(&emptyA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
+                    !mbar_wait(&emptyA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY | (71 << 4))) { ok_run = false; break; }
                 // records of the new input rows: thread pt builds conv pixels u = 2p and 2p + 1
                 // (p = pt % 64) of M-tile pt / 64, as tile rows p and p + 64 (the epilogue maps lane L
                 // back to pixel 2L or 2(L - 64) + 1); their 8-byte windows start at ring bytes 2 cx and
@@ -309,8 +309,8 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 const int b = i & 1;
                 const int slot = cr % 3;
                 // the slot held conv row cr - 3, last read by a pooling done while finishing row i - 1
-                if (i > 0 && !mbar_wait(&done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY)) { ok_run = false; break; }
-                if (!mbar_wait(&accf[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
+                if (i > 0 && !mbar_wait(&done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY | (72 << 4))) { ok_run = false; break; }
+                if (!mbar_wait(&accf[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (73 << 4))) { ok_run = false; break; }
                 tc_fence_after();
                 // both M-tiles of the conv row (MT <= 2): their TMEM loads issued together, each (k, c)
                 // quad read once for both
@@ -368,7 +368,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 // after conv row 2 py + 1: pool pooled row py from conv rows 2py-1 .. 2py+1
                 const int py = (cr - 1) >> 1;
                 if ((cr & 1) == 1 && py >= py0) {
-                    if (!mbar_wait(&written[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC)) { ok_run = false; break; }
+                    if (!mbar_wait(&written[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (74 << 4))) { ok_run = false; break; }
                     for (int px = px0; px < PW; px += 128) {
                         // per-byte max of the 9 taps as u16x2 max of the even and the odd bytes of
                         // every word (one native instruction each; a 4-byte SIMD max is not native)
