@@ -66,8 +66,9 @@ def parse():
                    help="only the config-1 micro-benchmark: one JSON line with every shape (ours, or with "
                         "--impl reference the reference's own sm_100 kernels), then exit")
     p.add_argument("--kernel", default=None, metavar="KIND:BLOCK:LAYER:N",
-                   help="profiling aid: 3 + 1 launches of one kernel (conv1 or conv2 of layer LAYER of "
-                        "block BLOCK, 0-based, on N images of random activations), then exit")
+                   help="profiling aid: 3 + 1 launches of one kernel (conv1 / conv2 of layer LAYER of "
+                        "block BLOCK, 0-based, trans of block BLOCK, or stem, on N images of random "
+                        "activations in the engine's tile-major layout), then exit")
     return p.parse_args()
 
 
@@ -523,8 +524,10 @@ def layers_summary(rows: list) -> dict:
 
 
 def one_kernel(spec: str, img: int) -> None:
-    """Launches one dense-layer kernel 3 + 1 times on random activations, with the tables of a
-    seeded random DenseNet169 calibrated on synthetic batches (a small, fixed case for ncu)."""
+    """Launches one kernel 3 + 1 times on random activations in the engine's layouts (tile-major
+    block store), with the tables of a seeded random DenseNet169 calibrated on synthetic batches (a
+    small, fixed case for ncu): conv1 / conv2 of layer LAYER of block BLOCK, the transition of block
+    BLOCK, or the stem (BLOCK and LAYER unused) on N images."""
     import numpy as np
     import torch
     from rsna_knee_efficiency_b200 import densenet, ops, quant, synth
@@ -537,25 +540,45 @@ def one_kernel(spec: str, img: int) -> None:
     par = quant.kernel_params(plan)
     blk = plan.blocks[bi]
     hw, rows = blk.h * blk.w, n * blk.h * blk.w
-    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    tiles = -(-rows // 128)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()    # noqa: E731
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    Gt = blk.c_tot // 32
     if kind == "conv1":
         cin = blk.c0 + 32 * li
-        in0 = torch.randint(-127, 128, (rows * blk.c0,), dtype=torch.int8, device="cuda")
-        seg = torch.randint(-127, 128, (max(li, 1) * rows * 32,), dtype=torch.int8, device="cuda")
+        store = torch.randint(-127, 128, (tiles * Gt * 4096,), dtype=torch.int8, device="cuda")
         out = torch.empty(rows * 128, dtype=torch.uint8, device="cuda")
         w1 = dev(ops.prepare_conv1_weights(par[f"L{bi}_{li}_w1"]))
         ab, gd = dev(par[f"L{bi}_{li}_abh"]), dev(par[f"L{bi}_{li}_gdu"])
         for _ in range(4):
-            ops.conv1(in0, seg, w1, ab, gd, out, blk.c0 // 32, cin // 32, n, hw, True, err=err)
+            ops.conv1(store, None, w1, ab, gd, out, blk.c0 // 32, cin // 32, n, hw, True, err=err, tile_groups=Gt)
     elif kind == "conv2":
         x = torch.randint(0, 80, (rows * 128,), dtype=torch.uint8, device="cuda")
-        out = torch.empty(rows * 32, dtype=torch.int8, device="cuda")
+        store = torch.empty(tiles * Gt * 4096, dtype=torch.int8, device="cuda")
         w2, sc = dev(ops.prepare_conv2_weights(par[f"L{bi}_{li}_w2k"])), dev(par[f"L{bi}_{li}_c2u"])
         for _ in range(4):
-            ops.conv2(x, w2, sc, out, n, blk.h, blk.w, err=err)
+            ops.conv2(x, w2, sc, store, n, blk.h, blk.w, err=err, tile_groups=Gt, group=blk.c0 // 32 + li)
+    elif kind == "trans":
+        nxt = plan.blocks[bi + 1]
+        store = torch.randint(-127, 128, (tiles * Gt * 4096,), dtype=torch.int8, device="cuda")
+        Gn = nxt.c_tot // 32
+        out = torch.empty(-(-(rows // 4) // 128) * Gn * 4096, dtype=torch.int8, device="cuda")
+        tw = dev(ops.prepare_trans_weights(par[f"T{bi}_w"]))
+        ab, gd = dev(par[f"T{bi}_abh"]), dev(par[f"T{bi}_gd"])
+        for _ in range(4):
+            ops.trans(store, None, tw, ab, gd, out, blk.c0 // 32, Gt, n, blk.h, blk.w, True, err=err,
+                      tile_groups=Gt, out_tile_groups=Gn)
+    elif kind == "stem":
+        b0 = plan.blocks[0]
+        planes = torch.from_numpy(synth.volume(3, H=img, W=img)).cuda()
+        src = torch.tensor([[i % 24, i % 24 + 1, i % 24 + 2, 0] for i in range(n)], dtype=torch.int32).cuda()
+        G0t = b0.c_tot // 32
+        out = torch.empty(-(-(n * b0.h * b0.w) // 128) * G0t * 4096, dtype=torch.int8, device="cuda")
+        w8, kc = dev(ops.prepare_stem_weights(par["S_w8"])), dev(par["S_kc"])
+        for _ in range(4):
+            ops.stem(planes, w8, kc, out, n, img, img, src=src, err=err, tile_groups=G0t)
     else:
-        raise SystemExit(f"--kernel: unknown kind {kind!r} (conv1 or conv2)")
+        raise SystemExit(f"--kernel: unknown kind {kind!r} (conv1, conv2, trans or stem)")
     torch.cuda.synchronize()
     if int(err.item()) != 0:
         raise SystemExit(f"--kernel {spec}: device error {int(err.item())}")
