@@ -23,9 +23,13 @@
 //              64 + u / 2) in a ring of 10 input rows;
 //   warp 0     TMEM owner / MMA issuer: per conv row and M-tile, 7 M128 N64 K32 MMAs (one per
 //              kernel row, A = that input row's records) into one of two TMEM accumulators;
-//   warps 5-12 (a lane quadrant x a 32-channel half each) requantise into a 3-row ring of conv
-//              outputs; after every odd conv row 2 py + 1 they max-pool pooled row py (conv rows
-//              2py-1 .. 2py+1) and write it out.
+//   warps 5-12 (a lane quadrant x a 32-channel half each) requantise their conv pixel's 32
+//              channels of each conv row and max-pool as the rows come: each thread owns one conv
+//              column (TMEM lane) of every conv row, so the vertical max over conv rows 2py-1 ..
+//              2py+1 runs in its registers (16-bit pairs: one vmax2 per two values); the horizontal
+//              max over columns 2px-1 .. 2px+1 takes the odd columns' pair max (lane quadrants 2-3:
+//              a shuffle, and one edge value across warps) to the even column's thread (quadrants
+//              0-1) through a double-buffered exchange in shared memory, which writes the pooled row.
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
@@ -37,13 +41,14 @@ constexpr int ST_RING = 16;               // input row ring
 constexpr int ST_KSTEPS = 7;
 constexpr int ST_WBYTES = ST_KSTEPS * 64 * 32;   // prepared weights [7][64][32] swizzled
 constexpr int ST_REC = 10;                // record ring: input rows y at slot y mod 10
+constexpr int MT_MAX = 2;                 // M-tiles of 128 conv pixels per conv row (W <= 512)
 
 struct StemGeo {
     int N, H, W;                           // input
     int CH, CW, PH, PW;                    // conv / pooled output
     int mt;                                // M-tiles per conv row
     int row_bytes;                         // one ring row of one channel: W + 8
-    size_t ring_off, rec_off, conv_off, bar_off, smem;
+    size_t ring_off, rec_off, xo_off, bar_off, smem;
 };
 
 static StemGeo stem_geo(int N, int H, int W) {
@@ -56,7 +61,7 @@ static StemGeo stem_geo(int N, int H, int W) {
     g.ring_off = off; off += static_cast<size_t>(ST_RING) * 3 * g.row_bytes;
     off = (off + 1023) / 1024 * 1024;
     g.rec_off = off; off += static_cast<size_t>(ST_REC) * g.mt * 4096;        // record ring
-    g.conv_off = off; off += static_cast<size_t>(3) * g.mt * 128 * 64;        // 3 conv rows
+    g.xo_off = off; off += static_cast<size_t>(2) * 2 * MT_MAX * 64 * 64 + 2 * 2 * 2 * MT_MAX * 64;   // exchange, edges
     g.bar_off = off; off += 256 + 1024;                                       // kc, barriers
     g.smem = off + 1024;
     return g;
@@ -69,7 +74,10 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     uint8_t* sW = smem;
     uint8_t* sRing = smem + geo.ring_off;
     uint8_t* sRec = smem + geo.rec_off;
-    uint8_t* sC = smem + geo.conv_off;
+    // pooling exchange: odd-column pair maxima [parity][half][M-tile][64 pooled px][16 u16x2 words],
+    // then the edge values of lane 31 of quadrants 2 / 3 [parity][half][quadrant - 2][M-tile][16]
+    uint32_t* sXo = reinterpret_cast<uint32_t*>(smem + geo.xo_off);
+    uint32_t* sXe = sXo + 2 * 2 * MT_MAX * 64 * 16;
     float* sKC = reinterpret_cast<float*>(smem + geo.bar_off);               // [128] k, c
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + geo.bar_off + 512);
     uint64_t* fullA = bars;          // [2] the records of conv row i ready (4 producer warps)
@@ -78,9 +86,10 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     uint64_t* acce = bars + 6;       // [2] (4 epilogue warps)
     uint64_t* wfull = bars + 8;      // weights landed
     uint64_t* ringrdy = bars + 9;    // [2] input rows of conv row i loaded (4 producer warps)
-    uint64_t* written = bars + 11;   // [2] conv row i in the conv ring (4 epilogue warps)
-    uint64_t* done = bars + 13;      // [2] conv row i finished, pooling included (4 epilogue warps)
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* eready = bars + 11;    // [2] pooled row k: the edge values published (4 odd-column warps)
+    uint64_t* xready = bars + 13;    // [2] pooled row k: the odd columns' pair maxima written (4 warps)
+    uint64_t* xfree = bars + 15;     // [2] pooled row k: the exchange read (4 even-column warps)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 17);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -97,8 +106,9 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             mbar_init(&accf[k], 1);
             mbar_init(&acce[k], 8);
             mbar_init(&ringrdy[k], 4);
-            mbar_init(&written[k], 8);
-            mbar_init(&done[k], 8);
+            mbar_init(&eready[k], 4);
+            mbar_init(&xready[k], 4);
+            mbar_init(&xfree[k], 4);
         }
         mbar_init(&wfull[0], 1);
         *s_abort = 0;
@@ -292,128 +302,139 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             if (!ok_run) break;
         }
     } else {
-        // ---------------- epilogue: requantise, ring, max-pool ----------------
-        // 8 warps: warp w reads TMEM lanes 32 (w % 4) .. + 31 (conv pixels) and channel half hc;
-        // the pooling splits the pooled pixels x channel halves (= the two output groups) likewise.
+        // ---------------- epilogue: requantise, max-pool ----------------
+        // 8 warps: warp w reads TMEM lanes 32 (w % 4) .. + 31 (tile rows: conv pixels) and channel
+        // half hc. Tile row r holds conv column 2r (r < 64) or 2(r - 64) + 1 (r >= 64) of each M-tile.
         const int quad = warp & 3, hc = (warp - 5) >> 2;
-        const int et = threadIdx.x - 160;                 // 0..255
-        const int pxh = et & 1, px0 = et >> 1;            // pooling: channel half, first pooled pixel
+        const int row = quad * 32 + lane;
+        const bool odd = row >= 64;                       // odd conv columns (quadrants 2, 3)
+        const int pl = odd ? row - 64 : row;              // pooled pixel within the M-tile
         const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
-        int i = 0;
+        // q = rint(clamp(fmaf(acc, k, c), 0, 127)) of channels 2j, 2j + 1 as the 16-bit pair (q0, q1);
+        // (k, c) of the pair from shared memory (the warp reads one address: a broadcast)
+        const float2* k2p = reinterpret_cast<const float2*>(sKC + hc * 32);
+        const float2* c2p = reinterpret_cast<const float2*>(sKC + 64 + hc * 32);
+        auto requant2 = [&](uint32_t v0, uint32_t v1, int j) -> uint32_t {
+            const float f0 = fast_cvt ? __uint_as_float(v0 + ACC_MAGIC) - ACC_MAGIC_F : __int2float_rn(static_cast<int32_t>(v0));
+            const float f1 = fast_cvt ? __uint_as_float(v1 + ACC_MAGIC) - ACC_MAGIC_F : __int2float_rn(static_cast<int32_t>(v1));
+            float t0, t1;
+            f2_unpack(f2_fma(f2_pack(f0, f1), k2p[j], c2p[j]), t0, t1);
+            const uint32_t b0 = __float_as_uint(fminf(fmaxf(t0, 0.0f), 127.0f) + 12582912.0f);
+            const uint32_t b1 = __float_as_uint(fminf(fmaxf(t1, 0.0f), 127.0f) + 12582912.0f);
+            return __byte_perm(b0, b1, 0x5410);           // the low byte of each: (q0, 0, q1, 0)
+        };
+        uint32_t acc[MT_MAX][16];                         // running vertical max of the pooled row
+        int i = 0, k = 0;                                 // conv rows, pooled rows of this CTA
         for (int t = 0; t < my_tasks; ++t) {
             int n, py0, cr0, nrows;
             task_rows(t, n, py0, cr0, nrows);
+#pragma unroll
+            for (int m = 0; m < MT_MAX; ++m)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[m][j] = 0u;   // the pad row above the image (values >= 0)
             bool ok_run = true;
             for (int r = 0; r < nrows; ++r, ++i) {
                 const int cr = cr0 + r;
                 const int b = i & 1;
-                const int slot = cr % 3;
-                // the slot held conv row cr - 3, last read by a pooling done while finishing row i - 1
-                if (i > 0 && !mbar_wait(&done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY | (72 << 4))) { ok_run = false; break; }
                 if (!mbar_wait(&accf[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (73 << 4))) { ok_run = false; break; }
                 tc_fence_after();
-                // both M-tiles of the conv row (MT <= 2): their TMEM loads issued together, each (k, c)
-                // quad read once for both
-                const int row = quad * 32 + lane;              // tile row -> conv pixel (see im2col)
-                const int cxr = row < 64 ? 2 * row : 2 * (row - 64) + 1;
                 const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * 128 + hc * 32;
-                uint32_t v0[32], v1[32];
-                tmem_ld32(tbase, v0);
-                if (MT > 1) tmem_ld32(tbase + 64, v1);
-                tmem_wait_ld(v0);
-                reg_bind(v1);
-                // q = rint(clamp(fmaf(acc, k, c), 0, 127)) of 4 channels as the bytes of one word
-                auto requant4 = [&](const uint32_t (&v)[32], int j, const float4& k4, const float4& c4) -> uint32_t {
-                    float f[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        f[e] = fast_cvt ? __uint_as_float(v[4 * j + e] + ACC_MAGIC) - ACC_MAGIC_F
-                                        : __int2float_rn(static_cast<int32_t>(v[4 * j + e]));
-                    float tq[4];
-                    f2_unpack(f2_fma(f2_pack(f[0], f[1]), f2_pack(k4.x, k4.y), f2_pack(c4.x, c4.y)), tq[0], tq[1]);
-                    f2_unpack(f2_fma(f2_pack(f[2], f[3]), f2_pack(k4.z, k4.w), f2_pack(c4.z, c4.w)), tq[2], tq[3]);
-                    uint32_t bq[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        bq[e] = __float_as_uint(fminf(fmaxf(tq[e], 0.0f), 127.0f) + 12582912.0f);
-                    return __byte_perm(__byte_perm(bq[0], bq[1], 0x0040), __byte_perm(bq[2], bq[3], 0x0040), 0x5410);
-                };
-                uint32_t wd0[8], wd1[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    // k, c of the 4 channels (broadcast reads); fmaf pairwise in f32x2
-                    const float4 k4 = *reinterpret_cast<const float4*>(sKC + hc * 32 + 4 * j);
-                    const float4 c4 = *reinterpret_cast<const float4*>(sKC + 64 + hc * 32 + 4 * j);
-                    wd0[j] = requant4(v0, j, k4, c4);
-                    wd1[j] = MT > 1 ? requant4(v1, j, k4, c4) : 0u;
-                }
-                // conv ring [3][MT][128 tile rows][64 B], by tile row; chunk j of row r at (j ^ (r & 3))
-                // spreads the banks
-                auto put_row = [&](int m, const uint32_t (&wd)[8]) {
-                    if (m * 128 + cxr >= CW) return;
-                    uint8_t* cp = sC + (static_cast<size_t>(slot) * MT * 128 + m * 128 + row) * 64;
-#pragma unroll
-                    for (int j = 0; j < 2; ++j)
-                        *reinterpret_cast<uint4*>(cp + (((2 * hc + j) ^ (row & 3)) << 4)) =
-                            make_uint4(wd[4 * j], wd[4 * j + 1], wd[4 * j + 2], wd[4 * j + 3]);
-                };
-                put_row(0, wd0);
-                if (MT > 1) put_row(1, wd1);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&acce[b]);
-                    mbar_arrive(&written[i & 1]);
-                }
-                // after conv row 2 py + 1: pool pooled row py from conv rows 2py-1 .. 2py+1
+                // conv row 2 py + 1 closes pooled row py (rows 2py-1 .. 2py+1) and opens py + 1
+                const bool closes = (cr & 1) == 1;
                 const int py = (cr - 1) >> 1;
-                if ((cr & 1) == 1 && py >= py0) {
-                    if (!mbar_wait(&written[i & 1], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (74 << 4))) { ok_run = false; break; }
-                    for (int px = px0; px < PW; px += 128) {
-                        // per-byte max of the 9 taps as u16x2 max of the even and the odd bytes of
-                        // every word (one native instruction each; a 4-byte SIMD max is not native)
-                        uint32_t mxe[8], mxo[8];
+                uint32_t fin[MT_MAX][16];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) mxe[j] = mxo[j] = 0u;
+                for (int m = 0; m < MT_MAX; ++m) {             // one M-tile's 32 columns at a time
+                    if (m < MT) {
+                        uint32_t v[32];
+                        tmem_ld32(tbase + m * 64, v);
+                        tmem_wait_ld(v);
 #pragma unroll
-                        for (int dy = -1; dy <= 1; ++dy) {
-                            const int cyy = 2 * py + dy;
-                            if (cyy < 0 || cyy >= CH) continue;
-                            const uint8_t* rowp = sC + static_cast<size_t>(cyy % 3) * MT * 128 * 64;
-#pragma unroll
-                            for (int dx = -1; dx <= 1; ++dx) {
-                                const int cxx = 2 * px + dx;
-                                if (cxx < 0 || cxx >= CW) continue;
-                                const int u = cxx & 127;
-                                const int trow = (u & 1) ? 64 + (u >> 1) : (u >> 1);
-                                const uint8_t* pp = rowp + ((cxx >> 7) * 128 + trow) * 64;
-#pragma unroll
-                                for (int j = 0; j < 2; ++j) {
-                                    const uint4 q = *reinterpret_cast<const uint4*>(pp + (((2 * pxh + j) ^ (trow & 3)) << 4));
-                                    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                                    for (int k = 0; k < 4; ++k) {
-                                        mxe[4 * j + k] = __vmaxu2(mxe[4 * j + k], __byte_perm(qw[k], 0u, 0x4240));
-                                        mxo[4 * j + k] = __vmaxu2(mxo[4 * j + k], __byte_perm(qw[k], 0u, 0x4341));
-                                    }
-                                }
-                            }
+                        for (int j = 0; j < 16; ++j) {
+                            const uint32_t w = requant2(v[2 * j], v[2 * j + 1], j);
+                            fin[m][j] = __vmaxu2(acc[m][j], w);
+                            acc[m][j] = closes ? w : fin[m][j];
                         }
-                        // block 1 input, group-major [2][N][PH * PW][32] (this half is group pxh), or
-                        // groups 0 / 1 of the tile-major block store
-                        const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
-                        int8_t* o = a.tile_groups > 0
-                                        ? a.out + (((pix >> 7) * a.tile_groups + pxh) << 12) + (pix & 127) * 32
-                                        : a.out + pxh * gstride + pix * 32;
-                        uint32_t mx[8];
+                    } else {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) mx[j] = __byte_perm(mxe[j], mxo[j], 0x6240);
-                        *reinterpret_cast<uint4*>(o) = make_uint4(mx[0], mx[1], mx[2], mx[3]);
-                        *reinterpret_cast<uint4*>(o + 16) = make_uint4(mx[4], mx[5], mx[6], mx[7]);
+                        for (int j = 0; j < 16; ++j) fin[m][j] = 0u;
                     }
                 }
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&done[i & 1]);
+                if (lane == 0) mbar_arrive(&acce[b]);          // the accumulator is free
+                if (!closes || py < py0) continue;
+                // ---- pooled row py: horizontal max over conv columns 2px - 1 .. 2px + 1 ----
+                const int par = k & 1, ph = (k >> 1) & 1;
+                ++k;
+                uint32_t* xo = sXo + (par * 2 + hc) * MT_MAX * 64 * 16;
+                uint32_t* xe = sXe + (par * 2 + hc) * 2 * MT_MAX * 16;
+                if (odd) {
+                    // the exchange of pooled row k - 2 (same parity) has been read
+                    if (!mbar_wait(&xfree[par], ph ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (75 << 4))) { ok_run = false; break; }
+                    if (lane == 31) {                          // columns m 128 + 63 (quad 2), m 128 + 127 (quad 3)
+#pragma unroll
+                        for (int m = 0; m < MT_MAX; ++m)
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4)
+                                *reinterpret_cast<uint4*>(xe + ((quad - 2) * MT_MAX + m) * 16 + j) =
+                                    make_uint4(fin[m][j], fin[m][j + 1], fin[m][j + 2], fin[m][j + 3]);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&eready[par]);
+                    if (!mbar_wait(&eready[par], ph, a.err, s_abort, ERR_WAIT_FULL | (76 << 4))) { ok_run = false; break; }
+                    // left neighbour (column 2 pl - 1 of the M-tile): lane - 1, or quad 2's lane 31 (for
+                    // quad 3) / quad 3's lane 31 of the previous M-tile (for quad 2; the pad before column 0)
+#pragma unroll
+                    for (int m = 0; m < MT_MAX; ++m) {
+                        const uint32_t* edge = quad == 3 ? xe + (0 * MT_MAX + m) * 16
+                                                         : (m > 0 ? xe + (1 * MT_MAX + m - 1) * 16 : nullptr);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            uint32_t left = __shfl_up_sync(0xffffffffu, fin[m][j], 1);
+                            if (lane == 0) left = edge != nullptr ? edge[j] : 0u;
+                            fin[m][j] = __vmaxu2(fin[m][j], left);
+                        }
+                        if (m < MT) {
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4)
+                                *reinterpret_cast<uint4*>(xo + (m * 64 + pl) * 16 + j) =
+                                    make_uint4(fin[m][j], fin[m][j + 1], fin[m][j + 2], fin[m][j + 3]);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xready[par]);
+                } else {
+                    if (!mbar_wait(&xready[par], ph, a.err, s_abort, ERR_WAIT_FULL | (77 << 4))) { ok_run = false; break; }
+#pragma unroll
+                    for (int m = 0; m < MT_MAX; ++m) {
+                        if (m >= MT) break;
+                        const int px = m * 64 + pl;
+                        uint32_t o[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            const uint4 q4 = *reinterpret_cast<const uint4*>(xo + (m * 64 + pl) * 16 + j);
+                            o[j] = q4.x; o[j + 1] = q4.y; o[j + 2] = q4.z; o[j + 3] = q4.w;
+                        }
+                        uint32_t mx[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            mx[j] = __byte_perm(__vmaxu2(fin[m][2 * j], o[2 * j]), __vmaxu2(fin[m][2 * j + 1], o[2 * j + 1]),
+                                                0x6420);
+                        if (px < PW) {
+                            // block 1 input, group-major [2][N][PH * PW][32] (this half is group hc), or
+                            // groups 0 / 1 of the tile-major block store
+                            const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
+                            int8_t* dst = a.tile_groups > 0
+                                              ? a.out + (((pix >> 7) * a.tile_groups + hc) << 12) + (pix & 127) * 32
+                                              : a.out + hc * gstride + pix * 32;
+                            *reinterpret_cast<uint4*>(dst) = make_uint4(mx[0], mx[1], mx[2], mx[3]);
+                            *reinterpret_cast<uint4*>(dst + 16) = make_uint4(mx[4], mx[5], mx[6], mx[7]);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xfree[par]);
+                }
             }
             if (!ok_run) break;
         }
