@@ -310,19 +310,25 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         const bool odd = row >= 64;                       // odd conv columns (quadrants 2, 3)
         const int pl = odd ? row - 64 : row;              // pooled pixel within the M-tile
         const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
-        // q = rint(clamp(fmaf(acc, k, c), 0, 127)) of channels 2j, 2j + 1 as the 16-bit pair (q0, q1);
-        // (k, c) of the pair from shared memory (the warp reads one address: a broadcast)
-        const float2* k2p = reinterpret_cast<const float2*>(sKC + hc * 32);
-        const float2* c2p = reinterpret_cast<const float2*>(sKC + 64 + hc * 32);
-        auto requant2 = [&](uint32_t v0, uint32_t v1, int j) -> uint32_t {
-            const float f0 = fast_cvt ? __uint_as_float(v0 + ACC_MAGIC) - ACC_MAGIC_F : __int2float_rn(static_cast<int32_t>(v0));
-            const float f1 = fast_cvt ? __uint_as_float(v1 + ACC_MAGIC) - ACC_MAGIC_F : __int2float_rn(static_cast<int32_t>(v1));
-            float t0, t1;
-            f2_unpack(f2_fma(f2_pack(f0, f1), k2p[j], c2p[j]), t0, t1);
-            const uint32_t b0 = __float_as_uint(fminf(fmaxf(t0, 0.0f), 127.0f) + 12582912.0f);
-            const uint32_t b1 = __float_as_uint(fminf(fmaxf(t1, 0.0f), 127.0f) + 12582912.0f);
-            return __byte_perm(b0, b1, 0x5410);           // the low byte of each: (q0, 0, q1, 0)
+        // q = rint(clamp(fmaf(acc, k, c), 0, 127)) of channels 2j, 2j + 1 as the 16-bit pair (q0, q1), with
+        // (k, c) of the pair given: int -> float through the magic add (both lanes in one packed add),
+        // the packed fma, the clamp, the rounding add of 1.5 * 2^23 (packed) whose low byte is q
+        const float2 mneg = make_float2(-ACC_MAGIC_F, -ACC_MAGIC_F), mrnd = make_float2(12582912.0f, 12582912.0f);
+        auto requant2 = [&](uint32_t v0, uint32_t v1, float2 k2, float2 c2) -> uint32_t {
+            float2 f;
+            if (fast_cvt) {
+                f = __fadd2_rn(make_float2(__uint_as_float(v0 + ACC_MAGIC), __uint_as_float(v1 + ACC_MAGIC)), mneg);
+            } else {
+                f = make_float2(__int2float_rn(static_cast<int32_t>(v0)), __int2float_rn(static_cast<int32_t>(v1)));
+            }
+            float2 t = f2_fma(f, k2, c2);
+            t.x = fminf(fmaxf(t.x, 0.0f), 127.0f);
+            t.y = fminf(fmaxf(t.y, 0.0f), 127.0f);
+            t = __fadd2_rn(t, mrnd);
+            return __byte_perm(__float_as_uint(t.x), __float_as_uint(t.y), 0x5410);   // (q0, 0, q1, 0)
         };
+        const float4* k4p = reinterpret_cast<const float4*>(sKC + hc * 32);
+        const float4* c4p = reinterpret_cast<const float4*>(sKC + 64 + hc * 32);
         uint32_t acc[MT_MAX][16];                         // running vertical max of the pooled row
         int i = 0, k = 0;                                 // conv rows, pooled rows of this CTA
         for (int t = 0; t < my_tasks; ++t) {
@@ -344,20 +350,32 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 const int py = (cr - 1) >> 1;
                 uint32_t fin[MT_MAX][16];
 #pragma unroll
-                for (int m = 0; m < MT_MAX; ++m) {             // one M-tile's 32 columns at a time
-                    if (m < MT) {
-                        uint32_t v[32];
-                        tmem_ld32(tbase + m * 64, v);
-                        tmem_wait_ld(v);
+                for (int j = 0; j < 16; ++j) fin[MT_MAX - 1][j] = 0u;
+                // 16 channels (8 pairs) at a time, both M-tiles' columns with the same (k, c)
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const uint32_t w = requant2(v[2 * j], v[2 * j + 1], j);
-                            fin[m][j] = __vmaxu2(acc[m][j], w);
-                            acc[m][j] = closes ? w : fin[m][j];
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t v0[16], v1[16];
+                    tmem_ld16(tbase + h * 16, v0);
+                    if (MT > 1) tmem_ld16(tbase + 64 + h * 16, v1);
+                    tmem_wait_ld(v0);
+                    reg_bind(v1);
+#pragma unroll
+                    for (int jq = 0; jq < 4; ++jq) {
+                        const float4 k4 = k4p[h * 4 + jq], c4 = c4p[h * 4 + jq];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int jj = 2 * jq + e, j = h * 8 + jj;
+                            const float2 k2 = e ? make_float2(k4.z, k4.w) : make_float2(k4.x, k4.y);
+                            const float2 c2 = e ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+                            const uint32_t w0 = requant2(v0[2 * jj], v0[2 * jj + 1], k2, c2);
+                            fin[0][j] = __vmaxu2(acc[0][j], w0);
+                            acc[0][j] = closes ? w0 : fin[0][j];
+                            if (MT > 1) {
+                                const uint32_t w1 = requant2(v1[2 * jj], v1[2 * jj + 1], k2, c2);
+                                fin[1][j] = __vmaxu2(acc[1][j], w1);
+                                acc[1][j] = closes ? w1 : fin[1][j];
+                            }
                         }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) fin[m][j] = 0u;
                     }
                 }
                 tc_fence_before();
