@@ -30,6 +30,7 @@
 // warp 0 issues M = 256 MMAs over both CTAs (tcgen05 cta_group::2), the odd CTA's prologue and
 // epilogue warps arrive on the even CTA's fullA / acce, and commits arrive in both CTAs.
 #include <atomic>
+#include <type_traits>
 
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
@@ -120,6 +121,12 @@ static size_t gemm_layout(bool trans, bool pair, int G, int nc, int nchunks, int
     if (!trans && used <= SMEM_BUDGET) {
         int extra = static_cast<int>((SMEM_BUDGET - used) / raw_bytes);
         extra = extra > CONV1_SR_MAX - sr ? CONV1_SR_MAX - sr : extra;
+        // An even ring: slot s then only ever carries stages of one parity, i.e. of one of the two
+        // prologue warps of a lane quadrant, and that warp waits on the slot's phases one after the
+        // other. With an odd ring the other warp could start waiting on stage i while stage i - SR of
+        // the same slot (an earlier copy, not yet landed) is still the slot's open phase; a parity
+        // wait two phases ahead passes at once, and the warp would read the slot before its bytes.
+        extra &= ~1;
         *sr_out = sr + extra;
         used += static_cast<size_t>(extra) * raw_bytes;
     }
@@ -205,7 +212,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     int ok = 1;
     for (int i = threadIdx.x; i < a.cout; i += GM_THREADS) {
         const float2 p = reinterpret_cast<const float2*>(a.gd)[i];
-        sGd[i] = p;
+        if (TRANS) {
+            sGd[i] = p;
+        } else {                                      // conv1: (g0, g1, d0, d1) per channel pair
+            float* q = reinterpret_cast<float*>(sGd) + 4 * (i >> 1) + (i & 1);
+            q[0] = p.x;
+            q[2] = p.y;
+        }
         if (TRANS) ok &= (p.x * 4194304.0f >= 127.0f) ? 1 : 0;
         else ok &= (fmaf(p.x, 4194304.0f, p.y) >= 1.0f && fmaf(p.x, -4194304.0f, p.y) <= 0.0f) ? 1 : 0;
     }
@@ -562,86 +575,94 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     } else {
         // ---------------- epilogue ----------------
         // TMEM accumulators hold the int32 sums (each tile's first MMA overwrites); the int -> float
-        // conversion is an integer add of the MAGIC bits and one float subtraction.
+        // conversion is an integer add of the MAGIC bits and one float subtraction (one packed f32x2
+        // subtraction per channel pair; conv1's 255 v + 2^23 is one packed fma per pair as well).
         const int quad = warp & 3, half = (warp - 11) >> 2;
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
-        for (int t = 0; t < my_tiles; ++t) {
-            const int acc = t & 1;
-            if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (13 << 4), lim)) break;
-            tc_fence_after();
-            const int tile = unit + t * nunits;
-            const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
-            const int chunk = tile % nch;
-            const int ncol = min(NC, a.cout - chunk * NC) >> 1;      // columns of this warp
-            const int m = (tile / nch) * MT + static_cast<int>(rank) * 128 + quad * 32 + lane;
-            const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
-            // requantise 16 columns (output channels c0 ..) of this warp's 32 rows and store them
-            auto finish = [&](const uint32_t (&v)[16], int cb) {
-                const int c0 = chunk * NC + half * ncol + cb;      // first output channel (even)
-                const float4* gdp = gd4 + (c0 >> 1);               // (g, d) pairs of channels c0 ..
-                uint32_t wd[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    uint32_t b[4];
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int c = 4 * j + 2 * e;
-                        float f0, f1;
-                        if (fast_cvt) {
-                            f0 = __uint_as_float(v[c] + ACC_MAGIC) - ACC_MAGIC_F;
-                            f1 = __uint_as_float(v[c + 1] + ACC_MAGIC) - ACC_MAGIC_F;
-                        } else {
-                            f0 = __int2float_rn(static_cast<int32_t>(v[c]));
-                            f1 = __int2float_rn(static_cast<int32_t>(v[c + 1]));
+        // the conversion mode is fixed per launch: one instantiation of the tile loop per mode
+        auto tiles = [&](auto fast_tag) {
+            constexpr bool FAST = decltype(fast_tag)::value;
+            for (int t = 0; t < my_tiles; ++t) {
+                const int acc = t & 1;
+                if (!mbar_wait(&accf[acc], (t >> 1) & 1, a.err, s_abort, ERR_WAIT_ACC | (13 << 4), lim)) break;
+                tc_fence_after();
+                const int tile = unit + t * nunits;
+                const int nch = TRANS ? a.nchunks : 1;                   // conv1: one chunk
+                const int chunk = tile % nch;
+                const int ncol = min(NC, a.cout - chunk * NC) >> 1;      // columns of this warp
+                const int m = (tile / nch) * MT + static_cast<int>(rank) * 128 + quad * 32 + lane;
+                const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * NC + half * ncol;
+                // requantise 16 columns (output channels c0 ..) of this warp's 32 rows and store them
+                auto finish = [&](const uint32_t (&v)[16], int cb) {
+                    const int c0 = chunk * NC + half * ncol + cb;      // first output channel (even)
+                    const float4* gdp = gd4 + (c0 >> 1);               // (g, d) pairs of channels c0 ..
+                    uint32_t wd[4];
+    #pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t b[4];
+    #pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int c = 4 * j + 2 * e;
+                            float2 f;
+                            if constexpr (FAST) {
+                                f = __fadd2_rn(make_float2(__uint_as_float(v[c] + ACC_MAGIC), __uint_as_float(v[c + 1] + ACC_MAGIC)),
+                                               make_float2(-ACC_MAGIC_F, -ACC_MAGIC_F));
+                            } else {
+                                f = make_float2(__int2float_rn(static_cast<int32_t>(v[c])),
+                                                __int2float_rn(static_cast<int32_t>(v[c + 1])));
+                            }
+                            const float4 p = gdp[c >> 1];   // transition: (g0, d0, g1, d1); conv1: (g0, g1, d0, d1)
+                            float2 r;
+                            if (TRANS) {
+                                r.x = fminf(fmaxf(p.x * f.x, -127.0f), 127.0f) + 12582912.0f;
+                                r.y = fminf(fmaxf(p.z * f.y, -127.0f), 127.0f) + 12582912.0f;
+                            } else {
+                                // sat(g acc + d) per channel (one rounding each), then 255 v + 2^23 on the pair
+                                r = __ffma2_rn(make_float2(__saturatef(fmaf(p.x, f.x, p.z)), __saturatef(fmaf(p.y, f.y, p.w))),
+                                               make_float2(255.0f, 255.0f), make_float2(8388608.0f, 8388608.0f));
+                            }
+                            b[2 * e] = __float_as_uint(r.x);
+                            b[2 * e + 1] = __float_as_uint(r.y);
                         }
-                        const float4 p = gdp[c >> 1];                  // (g, d) of channels c0+c, c0+c+1
-                        float r0, r1;
-                        if (TRANS) {
-                            r0 = fminf(fmaxf(p.x * f0, -127.0f), 127.0f) + 12582912.0f;
-                            r1 = fminf(fmaxf(p.z * f1, -127.0f), 127.0f) + 12582912.0f;
-                        } else {
-                            r0 = fmaf(__saturatef(fmaf(p.x, f0, p.y)), 255.0f, 8388608.0f);
-                            r1 = fmaf(__saturatef(fmaf(p.z, f1, p.w)), 255.0f, 8388608.0f);
-                        }
-                        b[2 * e] = __float_as_uint(r0);
-                        b[2 * e + 1] = __float_as_uint(r1);
+                        wd[j] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
                     }
-                    wd[j] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+                    if (m < rows) {
+                        uint8_t* o = static_cast<uint8_t*>(a.out);
+                        // transition: next block input, group-major [c_out / 32][N * HW / 4][32] or groups
+                        // 0 .. c_out / 32 - 1 of its tile-major store; conv1: bottleneck planes of 16
+                        // channels [8][N * HW][16]
+                        size_t off;
+                        if (TRANS && a.tg_out > 0)
+                            off = ((static_cast<size_t>(m >> 7) * a.tg_out + (c0 >> 5)) << 12) + (m & 127) * 32 + (c0 & 16);
+                        else if (TRANS)
+                            off = (static_cast<size_t>(c0 >> 5) * rows + m) * 32 + (c0 & 16);
+                        else
+                            off = (static_cast<size_t>(c0 >> 4) * rows + m) * 16;
+                        *reinterpret_cast<uint4*>(o + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                    }
+                };
+                // 16-column chunks, each chunk's TMEM load issued one chunk ahead (tcgen05.wait::ld waits
+                // for every earlier load, so the load of chunk k + 1 is in flight while chunk k is worked)
+                uint32_t va[16], vb[16];
+                tmem_ld16(taddr, va);
+                for (int cb = 0; cb < ncol; cb += 32) {
+                    tmem_wait_ld(va);
+                    tmem_ld16(taddr + cb + 16, vb);
+                    finish(va, cb);
+                    tmem_wait_ld(vb);
+                    if (cb + 32 < ncol) tmem_ld16(taddr + cb + 32, va);
+                    finish(vb, cb + 16);
                 }
-                if (m < rows) {
-                    uint8_t* o = static_cast<uint8_t*>(a.out);
-                    // transition: next block input, group-major [c_out / 32][N * HW / 4][32] or groups
-                    // 0 .. c_out / 32 - 1 of its tile-major store; conv1: bottleneck planes of 16
-                    // channels [8][N * HW][16]
-                    size_t off;
-                    if (TRANS && a.tg_out > 0)
-                        off = ((static_cast<size_t>(m >> 7) * a.tg_out + (c0 >> 5)) << 12) + (m & 127) * 32 + (c0 & 16);
-                    else if (TRANS)
-                        off = (static_cast<size_t>(c0 >> 5) * rows + m) * 32 + (c0 & 16);
-                    else
-                        off = (static_cast<size_t>(c0 >> 4) * rows + m) * 16;
-                    *reinterpret_cast<uint4*>(o + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (PAIR) mbar_arrive_at(&acce[acc], 0);      // the issuing CTA's barrier
+                    else mbar_arrive(&acce[acc]);
                 }
-            };
-            // 16-column chunks, each chunk's TMEM load issued one chunk ahead (tcgen05.wait::ld waits
-            // for every earlier load, so the load of chunk k + 1 is in flight while chunk k is worked)
-            uint32_t va[16], vb[16];
-            tmem_ld16(taddr, va);
-            for (int cb = 0; cb < ncol; cb += 32) {
-                tmem_wait_ld(va);
-                tmem_ld16(taddr + cb + 16, vb);
-                finish(va, cb);
-                tmem_wait_ld(vb);
-                if (cb + 32 < ncol) tmem_ld16(taddr + cb + 32, va);
-                finish(vb, cb + 16);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if constexpr (PAIR) mbar_arrive_at(&acce[acc], 0);      // the issuing CTA's barrier
-                else mbar_arrive(&acce[acc]);
-            }
-        }
+        };
+        if (fast_cvt) tiles(std::true_type{});
+        else tiles(std::false_type{});
     }
 
     tc_fence_before();
