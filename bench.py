@@ -16,7 +16,9 @@ collective on the data path (weak scaling); the logits are gathered on the host.
 One JSON line (rank 0): `value` = images/s over all ranks with the study volumes resident in HBM;
 `e2e` = the same through the public API with the volumes copied from pinned host memory and the
 logits read back every step; `roofline` = the dominant kernel (conv1, all 82 layers) against the
-measured HBM copy bandwidth, with every kernel family in `roofline.network`; `sweep` = BASELINE
+measured HBM copy bandwidth, with every kernel family in `roofline.network` (`frac`: one pass profiled
+launch by launch; `step_frac`: the timed step, whose two seed passes overlap, against the same
+roofline time per pass); `sweep` = BASELINE
 config 4 (1, 4, 16, 64 studies per GPU per step); `layers` = BASELINE config 1 (one launch per
 layer shape on 24 images, summed per kernel and block); `cpu_baseline` = the CPU port of the
 reference's INT8 path on this host. `--impl reference` times that CPU port alone (rank 0; other
@@ -693,6 +695,11 @@ def main():
     imgs_per_study = imgs_per_step / S
     roof = roofline(runner, hbm, i8, peak_kind, vol_dev) if rank == 0 else None
     config_pass = runner.encoders[0].nb
+    if roof is not None:
+        # the whole step against its roofline: the step runs imgs_per_step / config_pass passes (the
+        # seeds' passes overlap on their streams), each with the profiled pass's roofline time
+        roof["network"]["step_frac"] = round(roof["network"]["roof_ms"] * imgs_per_step / config_pass
+                                             / (ms / args.steps), 4)
     device_mb = runner.encoders[0].device_mb
     launches = runner.launches_per_call * args.steps
     n_out = runner.n_out
@@ -715,7 +722,9 @@ def main():
                "e2e_images_per_s": round(r2.images_per_call * steps * world / (m2 * 1e-3), 1),
                "ms_per_step": round(m1 / steps, 3)}
         if rank == 0:
-            row["network_frac"] = roofline(r2, hbm, i8, peak_kind, vd)["network"]["frac"]
+            net = roofline(r2, hbm, i8, peak_kind, vd)["network"]
+            row["network_frac"] = net["frac"]
+            row["step_frac"] = round(net["roof_ms"] * r2.images_per_call / r2.encoders[0].nb / (m1 / steps), 4)
         sweep_out.append(row)
         for e in r2.encoders:
             e.close()

@@ -315,8 +315,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     } else if (warp == 1) {
         // ---------------- store producer ----------------
         // Lane 0 waits for the slot and posts the stage's bytes; lanes 0 .. gc - 1 then each issue
-        // one K group's copy (one instruction for the whole stage).
-        int i = 0;
+        // one K group's copy (one instruction for the whole stage). Stage i uses ring slot i % SR in
+        // its (i / SR)-th round, both kept as running counters (SR is a launch parameter for conv1).
+        int i = 0, rs = 0, rph = 0;
         for (int t = 0; t < my_tiles; ++t) {
             const int tile = unit + t * nunits;
             const int m0 = (tile / a.nchunks) * MT + static_cast<int>(rank) * 128;
@@ -347,11 +348,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
             }
             bool ok_run = true;
             for (int j = 0; j < NS; ++j, ++i) {
-                const int s = i % SR;
+                const int s = rs, ph = rph;
+                if (++rs == SR) {
+                    rs = 0;
+                    rph ^= 1;
+                }
                 const int gc = min(KSTEP, G - j * KSTEP);
                 int ok = 1;
                 if (lane == 0) {
-                    ok = mbar_wait(&freeR[s], ((i / SR) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (6 << 4), lim) ? 1 : 0;
+                    ok = mbar_wait(&freeR[s], ph ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (6 << 4), lim) ? 1 : 0;
                     if (ok) mbar_expect_tx(&fullR[s], bytes * gc);
                 }
                 if (!__shfl_sync(0xffffffffu, ok, 0)) { ok_run = false; break; }
@@ -421,15 +426,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         const int roff = (q * 32 + t1) * 32 + t0 * 8;     // this thread's first raw bytes in a unit
         int j = kk;                                   // stage index within the tile (i = t * NS + j)
         while (j >= NS) j -= NS;
+        int rs = kk, rph = 0;                         // raw slot i % SR and round parity (i / SR) & 1
         for (int i = kk; i < T; i += 2) {
-            const int s = i % SR, sa = i % SA;
+            const int s = rs, ph = rph, sa = i % SA;
+            rs += 2;                                  // SR is even: the slot wraps exactly at SR
+            if (rs >= SR) {
+                rs -= SR;
+                rph ^= 1;
+            }
             const int gc = min(KSTEP, G - j * KSTEP);
             const int j_this = j;
             j += 2;
             while (j >= NS) j -= NS;
             // (the lanes of the warp poll the same barrier and abort flag in lockstep, so they leave
             // together; tcgen05.st below is warp-collective)
-            if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL | (9 << 4), lim)) break;
+            if (!mbar_wait(&fullR[s], ph, a.err, s_abort, ERR_WAIT_FULL | (9 << 4), lim)) break;
             if (!mbar_wait(&emptyA[sa], ((i / SA) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (10 << 4), lim)) break;
             tc_fence_after();
             // res[16 h + 4 x + e]: unit x (K group), rows t/4 + 16 h (e < 2) and t/4 + 16 h + 8 (e >= 2),

@@ -67,6 +67,9 @@ static StemGeo stem_geo(int N, int H, int W) {
     return g;
 }
 
+// U8: the input is uint8 volume planes (a.x_u8), else fp16 windows; a template parameter, so the row
+// prefetch is a plain (predicated) load whose registers nothing reads until the row is put
+template <bool U8>
 __global__ void __launch_bounds__(ST_THREADS, 1)
 stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     extern __shared__ uint8_t smem_raw[];
@@ -194,7 +197,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             for (int ch = 0; ch < 3; ++ch) {
                 rv[ch] = make_uint2(0u, 0u);
                 if (inside) {
-                    if (a.x_u8) {
+                    if constexpr (U8) {
                         rv[ch].x = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.x) +
                                                                              (static_cast<size_t>(planes[ch]) * H + y) * W) + pt);
                     } else {
@@ -210,7 +213,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             const int flip = a.flags != nullptr ? (a.flags[n] & 1) : 0;
 #pragma unroll
             for (int ch = 0; ch < 3; ++ch) {
-                uint32_t v = a.x_u8 ? rv[ch].x : (u8_of_f16x2(rv[ch].x) | (u8_of_f16x2(rv[ch].y) << 16));
+                uint32_t v = U8 ? rv[ch].x : (u8_of_f16x2(rv[ch].x) | (u8_of_f16x2(rv[ch].y) << 16));
                 int col = 4 * pt;
                 if (flip) {
                     v = __byte_perm(v, 0, 0x0123);
@@ -224,7 +227,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         for (int t = 0; t < my_tasks; ++t) {
             int n, py0, cr0, nrows;
             task_rows(t, n, py0, cr0, nrows);
-            if (a.x_u8)
+            if constexpr (U8)
 #pragma unroll
                 for (int ch = 0; ch < 3; ++ch) planes[ch] = a.src[n * 4 + ch];
             bool ok_run = true;
@@ -473,11 +476,11 @@ cudaError_t launch_stem(const dn8_stem_args& a, int sms, cudaStream_t st) {
     const int ntask = a.N * bands;
     const int grid = ntask < sms ? ntask : sms;
     if (grid <= 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(stem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(geo.smem));
+    auto kern = a.x_u8 ? stem_kernel<true> : stem_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(geo.smem));
     if (e != cudaSuccess) return e;
     // the first kernel of a pass: its predecessor may be anything (a copy, an event wait)
-    return launch_pdl(false, stem_kernel, dim3(grid), dim3(ST_THREADS), geo.smem, st, a, geo);
+    return launch_pdl(false, kern, dim3(grid), dim3(ST_THREADS), geo.smem, st, a, geo);
 }
 
 }  // namespace dn8
