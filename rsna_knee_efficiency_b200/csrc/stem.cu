@@ -30,6 +30,8 @@
 //              max over columns 2px-1 .. 2px+1 takes the odd columns' pair max (lane quadrants 2-3:
 //              a shuffle, and one edge value across warps) to the even column's thread (quadrants
 //              0-1) through a double-buffered exchange in shared memory, which writes the pooled row.
+#include <type_traits>
+
 #include "dn8_common.cuh"
 #include "dn8_kernels.h"
 
@@ -40,7 +42,7 @@ constexpr int ST_BP = 16;                 // pooled rows per band
 constexpr int ST_RING = 16;               // input row ring
 constexpr int ST_KSTEPS = 7;
 constexpr int ST_WBYTES = ST_KSTEPS * 64 * 32;   // prepared weights [7][64][32] swizzled
-constexpr int ST_REC = 10;                // record ring: input rows y at slot y mod 10
+constexpr int ST_REC = 14;                // record ring: input rows y at slot y mod 14
 constexpr int MT_MAX = 2;                 // M-tiles of 128 conv pixels per conv row (W <= 512)
 
 struct StemGeo {
@@ -83,16 +85,17 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
     uint32_t* sXe = sXo + 2 * 2 * MT_MAX * 64 * 16;
     float* sKC = reinterpret_cast<float*>(smem + geo.bar_off);               // [128] k, c
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + geo.bar_off + 512);
-    uint64_t* fullA = bars;          // [2] the records of conv row i ready (4 producer warps)
-    uint64_t* emptyA = bars + 2;     // [2] MMA done with conv row i (by row parity)
-    uint64_t* accf = bars + 4;       // [2]
-    uint64_t* acce = bars + 6;       // [2] (4 epilogue warps)
-    uint64_t* wfull = bars + 8;      // weights landed
-    uint64_t* ringrdy = bars + 9;    // [2] input rows of conv row i loaded (4 producer warps)
-    uint64_t* eready = bars + 11;    // [2] pooled row k: the edge values published (4 odd-column warps)
-    uint64_t* xready = bars + 13;    // [2] pooled row k: the odd columns' pair maxima written (4 warps)
-    uint64_t* xfree = bars + 15;     // [2] pooled row k: the exchange read (4 even-column warps)
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 17);
+    // fullA / emptyA: slot i % 4 for conv row i (the producer runs up to four rows ahead of the MMA)
+    uint64_t* fullA = bars;          // [4] the records of conv row i ready (4 producer warps)
+    uint64_t* emptyA = bars + 4;     // [4] MMA done with conv row i
+    uint64_t* accf = bars + 8;       // [2]
+    uint64_t* acce = bars + 10;      // [2] (4 epilogue warps)
+    uint64_t* wfull = bars + 12;     // weights landed
+    uint64_t* ringrdy = bars + 13;   // [2] input rows of conv row i loaded (4 producer warps)
+    uint64_t* eready = bars + 15;    // [2] pooled row k: the edge values published (4 odd-column warps)
+    uint64_t* xready = bars + 17;    // [2] pooled row k: the odd columns' pair maxima written (4 warps)
+    uint64_t* xfree = bars + 19;     // [2] pooled row k: the exchange read (4 even-column warps)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 21);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -104,14 +107,16 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
 
     if (threadIdx.x == 0) {
         for (int k = 0; k < 2; ++k) {
-            mbar_init(&fullA[k], 4);
-            mbar_init(&emptyA[k], 1);
             mbar_init(&accf[k], 1);
             mbar_init(&acce[k], 8);
             mbar_init(&ringrdy[k], 4);
             mbar_init(&eready[k], 4);
             mbar_init(&xready[k], 4);
             mbar_init(&xfree[k], 4);
+        }
+        for (int k = 0; k < 4; ++k) {
+            mbar_init(&fullA[k], 4);
+            mbar_init(&emptyA[k], 1);
         }
         mbar_init(&wfull[0], 1);
         *s_abort = 0;
@@ -168,7 +173,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 for (int r = 0; r < nrows; ++r, ++i) {
                     const int b = i & 1, cr = cr0 + r;
                     if (!mbar_wait_w(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC | (66 << 4))) { ok_run = false; break; }
-                    if (!mbar_wait_w(&fullA[b], (i >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL | (67 << 4))) { ok_run = false; break; }
+                    if (!mbar_wait_w(&fullA[i & 3], (i >> 2) & 1, a.err, s_abort, ERR_WAIT_FULL | (67 << 4))) { ok_run = false; break; }
                     tc_fence_after();
                     for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -178,7 +183,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                             const uint64_t bd = sdesc(w0 + ky * 2048, 16, 256, LAYOUT_SW32);
                             umma_u8s8_w(tmem + b * 128 + m * 64, ad, bd, idesc, ky ? 1u : 0u);   // first overwrites
                         }
-                    umma_commit_w(&emptyA[b]);
+                    umma_commit_w(&emptyA[i & 3]);
                     umma_commit_w(&accf[b]);
                 }
             }
@@ -238,7 +243,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                 if (r == 0) {
                     // a new band reuses ring slots the previous conv row may still be reading: wait
                     // until every producer warp has finished that row's im2col tile
-                    if (i > 0 && !mbar_wait(&fullA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_FULL | (68 << 4))) {
+                    if (i > 0 && !mbar_wait(&fullA[(i - 1) & 3], ((i - 1) >> 2) & 1, a.err, s_abort, ERR_WAIT_FULL | (68 << 4))) {
                         ok_run = false;
                         break;
                     }
@@ -260,12 +265,12 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                     fetch(n, 2 * cr + 4, pre0);
                     fetch(n, 2 * cr + 5, pre1);
                 }
-                const int b = i & 1;
-                // the new records overwrite the slots last read by conv row i - 2 (and, at a band's
-                // first row, by conv row i - 1 too): wait until the MMAs of those rows are done
-                if (!mbar_wait(&emptyA[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (70 << 4))) { ok_run = false; break; }
+                // the new records overwrite the slots of input rows 2 cr - 12, 2 cr - 11, last read by
+                // conv row i - 4 (at a band's first row, slots of any earlier row: conv row i - 1, whose
+                // completion implies every earlier one's): wait until the MMAs of that row are done
+                if (!mbar_wait(&emptyA[i & 3], ((i >> 2) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (70 << 4))) { ok_run = false; break; }
                 if (r == 0 && i > 0 &&
-                    !mbar_wait(&emptyA[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, s_abort, ERR_WAIT_EMPTY | (71 << 4))) { ok_run = false; break; }
+                    !mbar_wait(&emptyA[(i - 1) & 3], ((i - 1) >> 2) & 1, a.err, s_abort, ERR_WAIT_EMPTY | (71 << 4))) { ok_run = false; break; }
                 // records of the new input rows: thread pt builds conv pixels u = 2p and 2p + 1
                 // (p = pt % 64) of M-tile pt / 64, as tile rows p and p + 64 (the epilogue maps lane L
                 // back to pixel 2L or 2(L - 64) + 1); their 8-byte windows start at ring bytes 2 cx and
@@ -274,9 +279,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                     const int m = pt >> 6, r0 = pt & 63;
                     const int wb = 2 * min(m * 128 + 2 * r0, CW - 2);  // pixels past the conv width: junk rows
                     const int swz = ((r0 >> 2) & 1) << 4;
-                    const int y_first = r == 0 ? 2 * cr - 3 : 2 * cr + 2;
-                    const int y_end = 2 * cr + 4;
-                    for (int y = y_first; y < y_end; ++y) {
+                    auto build = [&](int y) {
                         uint32_t w0v[6], w1v[6];
 #pragma unroll
                         for (int ch = 0; ch < 3; ++ch) {
@@ -296,11 +299,18 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         uint8_t* d1 = d0 + 64 * 32;
                         *reinterpret_cast<uint4*>(d1 + swz) = make_uint4(w1v[0], w1v[1], w1v[2], w1v[3]);
                         *reinterpret_cast<uint4*>(d1 + (swz ^ 16)) = make_uint4(w1v[4], w1v[5], 0u, 0u);
+                    };
+                    if (r == 0) {
+                        for (int y = 2 * cr - 3; y < 2 * cr + 4; ++y) build(y);
+                    } else {
+                        // the two new rows: independent loads and stores, issued together
+#pragma unroll
+                        for (int k2 = 0; k2 < 2; ++k2) build(2 * cr + 2 + k2);
                     }
                 }
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&fullA[b]);
+                if (lane == 0) mbar_arrive(&fullA[i & 3]);
             }
             if (!ok_run) break;
         }
@@ -317,9 +327,9 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         // (k, c) of the pair given: int -> float through the magic add (both lanes in one packed add),
         // the packed fma, the clamp, the rounding add of 1.5 * 2^23 (packed) whose low byte is q
         const float2 mneg = make_float2(-ACC_MAGIC_F, -ACC_MAGIC_F), mrnd = make_float2(12582912.0f, 12582912.0f);
-        auto requant2 = [&](uint32_t v0, uint32_t v1, float2 k2, float2 c2) -> uint32_t {
+        auto requant2 = [&](uint32_t v0, uint32_t v1, float2 k2, float2 c2, auto fast_tag) -> uint32_t {
             float2 f;
-            if (fast_cvt) {
+            if constexpr (decltype(fast_tag)::value) {
                 f = __fadd2_rn(make_float2(__uint_as_float(v0 + ACC_MAGIC), __uint_as_float(v1 + ACC_MAGIC)), mneg);
             } else {
                 f = make_float2(__int2float_rn(static_cast<int32_t>(v0)), __int2float_rn(static_cast<int32_t>(v1)));
@@ -332,6 +342,8 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         };
         const float4* k4p = reinterpret_cast<const float4*>(sKC + hc * 32);
         const float4* c4p = reinterpret_cast<const float4*>(sKC + 64 + hc * 32);
+        // the conversion mode is fixed per launch: one instantiation of the task loop per mode
+        auto tasks = [&](auto fast_tag) {
         uint32_t acc[MT_MAX][16];                         // running vertical max of the pooled row
         int i = 0, k = 0;                                 // conv rows, pooled rows of this CTA
         for (int t = 0; t < my_tasks; ++t) {
@@ -370,11 +382,11 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                             const int jj = 2 * jq + e, j = h * 8 + jj;
                             const float2 k2 = e ? make_float2(k4.z, k4.w) : make_float2(k4.x, k4.y);
                             const float2 c2 = e ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
-                            const uint32_t w0 = requant2(v0[2 * jj], v0[2 * jj + 1], k2, c2);
+                            const uint32_t w0 = requant2(v0[2 * jj], v0[2 * jj + 1], k2, c2, fast_tag);
                             fin[0][j] = __vmaxu2(acc[0][j], w0);
                             acc[0][j] = closes ? w0 : fin[0][j];
                             if (MT > 1) {
-                                const uint32_t w1 = requant2(v1[2 * jj], v1[2 * jj + 1], k2, c2);
+                                const uint32_t w1 = requant2(v1[2 * jj], v1[2 * jj + 1], k2, c2, fast_tag);
                                 fin[1][j] = __vmaxu2(acc[1][j], w1);
                                 acc[1][j] = closes ? w1 : fin[1][j];
                             }
@@ -459,6 +471,9 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             }
             if (!ok_run) break;
         }
+        };
+        if (fast_cvt) tasks(std::true_type{});
+        else tasks(std::false_type{});
     }
 
     tc_fence_before();
