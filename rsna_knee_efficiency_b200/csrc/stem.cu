@@ -20,7 +20,7 @@
 //              c + 4, four zero bytes either side; the next conv row's loads are issued before this
 //              row's records are built), build the records of the new input rows (ceil(CW / 128)
 //              M-tiles of 128 pixels x 32 bytes each, 32B-swizzled, pixel u of a tile in row u / 2 or
-//              64 + u / 2) in a ring of 10 input rows;
+//              64 + u / 2) in a ring of 14 input rows;
 //   warp 0     TMEM owner / MMA issuer: per conv row and M-tile, 7 M128 N64 K32 MMAs (one per
 //              kernel row, A = that input row's records) into one of two TMEM accumulators;
 //   warps 5-12 (a lane quadrant x a 32-channel half each) requantise their conv pixel's 32
@@ -322,6 +322,10 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         const int row = quad * 32 + lane;
         const bool odd = row >= 64;                       // odd conv columns (quadrants 2, 3)
         const int pl = odd ? row - 64 : row;              // pooled pixel within the M-tile
+        // the exchange row of pooled pixel pl holds its four 16-byte chunks rotated by pl / 2, so the
+        // eight 16-byte accesses of a shared-memory wavefront (pixels pl .. pl + 7, 64 bytes apart)
+        // cover all 32 banks
+        auto xsw = [&](int j) { return ((((j >> 2) + (pl >> 1)) & 3) << 2); };
         const size_t gstride = static_cast<size_t>(a.n_alloc > geo.N ? a.n_alloc : geo.N) * PH * PW * 32;
         // q = rint(clamp(fmaf(acc, k, c), 0, 127)) of channels 2j, 2j + 1 as the 16-bit pair (q0, q1), with
         // (k, c) of the pair given: int -> float through the magic add (both lanes in one packed add),
@@ -431,7 +435,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         if (m < MT) {
 #pragma unroll
                             for (int j = 0; j < 16; j += 4)
-                                *reinterpret_cast<uint4*>(xo + (m * 64 + pl) * 16 + j) =
+                                *reinterpret_cast<uint4*>(xo + (m * 64 + pl) * 16 + xsw(j)) =
                                     make_uint4(fin[m][j], fin[m][j + 1], fin[m][j + 2], fin[m][j + 3]);
                         }
                     }
@@ -446,7 +450,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                         uint32_t o[16];
 #pragma unroll
                         for (int j = 0; j < 16; j += 4) {
-                            const uint4 q4 = *reinterpret_cast<const uint4*>(xo + (m * 64 + pl) * 16 + j);
+                            const uint4 q4 = *reinterpret_cast<const uint4*>(xo + (m * 64 + pl) * 16 + xsw(j));
                             o[j] = q4.x; o[j + 1] = q4.y; o[j + 2] = q4.z; o[j + 3] = q4.w;
                         }
                         uint32_t mx[8];
