@@ -501,43 +501,59 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         const int pw = warp - 3;
         const int h = lane & 1;
         const int W = a.W, W2 = W >> 1;
-        for (int u = pw; u < T * UNITS; u += 8) {
-            const int i = u / UNITS, x = u - i * UNITS;
+        // warp pw always holds unit x = pw % 4 of the stages i = pw / 4, + 2, ...; the shared-memory
+        // offsets of its rows depend only on the tile, so they are computed once per tile, and the
+        // stage's tile t and K group j advance as running counters (i = t * NS + j)
+        const int x = pw & 3;
+        int t = 0, j = pw >> 2;
+        while (j >= NS) {
+            j -= NS;
+            ++t;
+        }
+        int off[8];
+        int t_off = -1;
+        for (int i = pw >> 2; i < T; i += 2) {
+            if (t != t_off) {
+                t_off = t;
+                if (TRANS) {
+                    // pooled pixel m0 + r -> global pooled row gr (= n * H/2 + oy) and column ox; its
+                    // input pixel (2 oy + dy, 2 ox + dx) sits 2W (gr - gr0) + dy W + 2 ox + dx pixels after
+                    // the first pixel of the copied span
+                    const int tile = unit + t * nunits;
+                    const int m0 = (tile / a.nchunks) * 128;
+                    const int gr0 = m0 / W2;
+                    const int first = 2 * W * gr0;                // first input pixel of the copied span
+                    int m = min(m0 + (lane >> 1), rows - 1);
+                    int gr = m / W2, ox = m - gr * W2;
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int rel = 2 * W * (gr - gr0) + (x >> 1) * W + 2 * ox + (x & 1);
+                        if (a.tg > 0) {                           // tile-major span: whole 4 KB tiles
+                            const int q = first + rel;
+                            off[jj] = ((q >> 7) - (first >> 7)) * 4096 + (q & 127) * 32 + h * 16;
+                        } else {
+                            off[jj] = rel * 32 + h * 16;
+                        }
+                        if (jj < 7) {                             // next chunk row: +16 pooled pixels
+                            const int step = min(16, rows - 1 - m);
+                            m += step;
+                            ox += step;
+                            while (ox >= W2) { ox -= W2; ++gr; }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) off[jj] = x * 4096 + (jj * 32 + lane) * 16;
+                }
+            }
             const int s = i % SR, sa = i % SA;
-            const int t = i / NS, j = i - t * NS;
             const int gc = min(KSTEP, G - j * KSTEP);
             const bool active = TRANS || x < gc;                  // conv1: the tile's last stage may be short
             const int g = TRANS ? j : j * KSTEP + x;              // K group of this unit
-            int off[8];
-            if (TRANS) {
-                // pooled pixel m0 + r -> global pooled row gr (= n * H/2 + oy) and column ox; its input
-                // pixel (2 oy + dy, 2 ox + dx) sits 2W (gr - gr0) + dy W + 2 ox + dx pixels after the
-                // first pixel of the copied span
-                const int tile = unit + t * nunits;
-                const int m0 = (tile / a.nchunks) * 128;
-                const int gr0 = m0 / W2;
-                const int first = 2 * W * gr0;                    // first input pixel of the copied span
-                int m = min(m0 + (lane >> 1), rows - 1);
-                int gr = m / W2, ox = m - gr * W2;
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    const int rel = 2 * W * (gr - gr0) + (x >> 1) * W + 2 * ox + (x & 1);
-                    if (a.tg > 0) {                               // tile-major span: whole 4 KB tiles
-                        const int q = first + rel;
-                        off[jj] = ((q >> 7) - (first >> 7)) * 4096 + (q & 127) * 32 + h * 16;
-                    } else {
-                        off[jj] = rel * 32 + h * 16;
-                    }
-                    if (jj < 7) {                         // next chunk row: +16 pooled pixels
-                        const int step = min(16, rows - 1 - m);
-                        m += step;
-                        ox += step;
-                        while (ox >= W2) { ox -= W2; ++gr; }
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) off[jj] = x * 4096 + (jj * 32 + lane) * 16;
+            j += 2;                                               // the next stage of this warp (NS >= 2)
+            while (j >= NS) {
+                j -= NS;
+                ++t;
             }
             if (!mbar_wait(&fullR[s], (i / SR) & 1, a.err, s_abort, ERR_WAIT_FULL | (11 << 4), lim)) break;
             uint4 q[8];
