@@ -211,8 +211,11 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
             uint32_t wd[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const uint4 el = *reinterpret_cast<const uint4*>(xq + ql * 32 + 4 * j);
-                const uint4 er = *reinterpret_cast<const uint4*>(xq + qr * 32 + 16 + 4 * j);
+                // the other quads' edge taps count only for lanes 0 / 31 inside the image row: the
+                // other lanes read nothing and add zero
+                uint4 el = make_uint4(0u, 0u, 0u, 0u), er = make_uint4(0u, 0u, 0u, 0u);
+                if (ex_l) el = *reinterpret_cast<const uint4*>(xq + ql * 32 + 4 * j);
+                if (ex_r) er = *reinterpret_cast<const uint4*>(xq + qr * 32 + 16 + 4 * j);
                 const uint32_t le[4] = {el.x, el.y, el.z, el.w};
                 const uint32_t re[4] = {er.x, er.y, er.z, er.w};
                 const float4 s4 = sc4[j];                             // broadcast read, 4 scales
@@ -220,8 +223,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
                 uint32_t q[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const int32_t accv = sum[4 * j + k] + (ex_l ? static_cast<int32_t>(le[k]) : 0) +
-                                         (ex_r ? static_cast<int32_t>(re[k]) : 0);
+                    const int32_t accv = sum[4 * j + k] + static_cast<int32_t>(le[k]) + static_cast<int32_t>(re[k]);
                     const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
                                              : __int2float_rn(accv);
                     // rint(clamp(f sc, +-127)) as the low byte of (clamped + 1.5 * 2^23)
