@@ -175,10 +175,11 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                     if (!mbar_wait_w(&acce[b], ((i >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC | (66 << 4))) { ok_run = false; break; }
                     if (!mbar_wait_w(&fullA[i & 3], (i >> 2) & 1, a.err, s_abort, ERR_WAIT_FULL | (67 << 4))) { ok_run = false; break; }
                     tc_fence_after();
+                    const int slot0 = ((2 * cr - 3) % ST_REC + ST_REC) % ST_REC;   // records of input row 2 cr - 3
                     for (int m = 0; m < MT; ++m)
 #pragma unroll
                         for (int ky = 0; ky < ST_KSTEPS; ++ky) {
-                            const int slot = ((2 * cr + ky - 3) % ST_REC + ST_REC) % ST_REC;   // input row's records
+                            const int slot = slot0 + ky < ST_REC ? slot0 + ky : slot0 + ky - ST_REC;   // input row's records
                             const uint64_t ad = sdesc(a0 + (slot * MT + m) * 4096, 16, 256, LAYOUT_SW32);
                             const uint64_t bd = sdesc(w0 + ky * 2048, 16, 256, LAYOUT_SW32);
                             umma_u8s8_w(tmem + b * 128 + m * 64, ad, bd, idesc, ky ? 1u : 0u);   // first overwrites
@@ -196,6 +197,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         // or four fp16 pixels, per channel and thread; the loads of a row are independent), then
         // put into ring slot y % ST_RING (column c at byte c + 4, flipped if asked).
         int planes[3] = {0, 0, 0};                        // uint8 planes of the task's image
+        int flip = 0;                                     // the task's image is flipped
         auto fetch = [&](int n, int y, uint2 (&rv)[3]) {
             const bool inside = y >= 0 && y < H && pt < W / 4;
 #pragma unroll
@@ -215,7 +217,6 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
         auto put = [&](int n, int y, const uint2 (&rv)[3]) {
             if (pt >= W / 4) return;
             uint8_t* dst = sRing + (y & (ST_RING - 1)) * 3 * RB + 4;
-            const int flip = a.flags != nullptr ? (a.flags[n] & 1) : 0;
 #pragma unroll
             for (int ch = 0; ch < 3; ++ch) {
                 uint32_t v = U8 ? rv[ch].x : (u8_of_f16x2(rv[ch].x) | (u8_of_f16x2(rv[ch].y) << 16));
@@ -235,6 +236,7 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
             if constexpr (U8)
 #pragma unroll
                 for (int ch = 0; ch < 3; ++ch) planes[ch] = a.src[n * 4 + ch];
+            flip = a.flags != nullptr ? (a.flags[n] & 1) : 0;      // per image
             bool ok_run = true;
             for (int r = 0; r < nrows; ++r, ++i) {
                 const int cr = cr0 + r;
