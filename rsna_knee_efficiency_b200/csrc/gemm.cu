@@ -1,8 +1,9 @@
 // gemm.cu -- the "prologue GEMM" kernels of the encoder on sm_100a: conv1 of every dense layer and
-// the transitions. Both read a block store whose 32-channel groups are all group-major,
-// [G][N][HW][32] int8 (block input groups first, then the layer segments), apply the consumer's
-// BatchNorm + ReLU + u8 quantisation (the prologue), multiply on tcgen05 (kind::i8,
-// u8 x s8 -> s32 in TMEM) and requantise in the epilogue.
+// the transitions. Both read a block store of 32-channel int8 groups -- group-major planes
+// [G][N][HW][32] (block input groups first, then the layer segments: the reference's layout, at the
+// kernel ABI) or tile-major [ceil(N HW / 128)][tg][128][32] (all groups of 128 consecutive pixels
+// contiguous: the engine's layout) -- apply the consumer's BatchNorm + ReLU + u8 quantisation (the
+// prologue), multiply on tcgen05 (kind::i8, u8 x s8 -> s32 in TMEM) and requantise in the epilogue.
 //
 //   conv1      : M = N*HW pixels, N = 128, K = c_in; out = rint(255 sat(g acc + d)) as the u8
 //                bottleneck planes [8][M][16] (reference conv1w_body, dense8s_kernels.cu:479-627).
@@ -10,7 +11,7 @@
 //                K group the four pixels of each 2x2 square are four A sub-tiles multiplied by the
 //                same weights into ONE accumulator: s = the sum of the four 1x1 outputs, exact in
 //                int32 (the integer form gemm_q MODE 1, :375-389); q = rint(clamp(k s, +-127)) into
-//                the next block's group-major input [c_out/32][N][HW/4][32].
+//                the next block's group-major input [c_out/32][N][HW/4][32] or tile-major store.
 //
 // Pipeline stage = 4 "units" of 128 rows x 32 bytes (16 KB of A, 4 MMAs M128 x NC x K32, one
 // commit): conv1 takes 4 consecutive K groups per stage, the transition the 4 pixels of each
@@ -19,7 +20,8 @@
 // arrive by bulk async copies into a shared-memory ring (explicit bytes in flight, no L1 staging).
 // Persistent, one CTA per SM, 19 warps:
 //   warp 0       TMEM owner and MMA issuer (the whole warp; one elected lane issues).
-//   warp 1       store producer: bulk copies into the raw ring (one lane per K group of a stage).
+//   warp 1       store producer: bulk copies into the raw ring (tile-major: one copy per stage;
+//                group-major: one lane per K group of a stage; the transition: one per 4 KB tile).
 //   warp 2       weight producer (lane 0): UMMA-ready weight tiles, resident when they fit.
 //   warps 3-10   prologue: raw ring -> BN/ReLU/u8 -> the A operand (conv1: TMEM, two warps per
 //                lane quadrant taking alternate stages; transition: one warp per unit, 32B-swizzled
