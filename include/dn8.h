@@ -17,6 +17,13 @@
  *    caller's stream without host synchronisation or allocation, so it can be captured in a CUDA
  *    graph. A handle is not thread-safe; distinct handles are independent.
  *
+ * Block stores. Activations (int8 q, 32-channel groups) are either the reference's group-major
+ * planes [G][N*HW][32] of signed bytes, or (tile_groups > 0 in the argument structs) a tile-major
+ * block store [ceil(N*HW/128)][tile_groups][128][32]: 128 consecutive pixels per tile, all of a
+ * tile's groups contiguous, each byte q + 128 (offset binary: the prologue's own input form, so
+ * its readers skip the sign flip of every byte). The engine keeps every block in that form;
+ * dn8_engine_store returns signed q.
+ *
  * Status codes: DN8_OK, DN8_EINVAL (bad argument or unsupported geometry; the reference raises
  * ValueError), DN8_ECUDA (CUDA runtime error; reference `cudart.CudaError`), DN8_EDEVICE (a kernel
  * reported an error through its error word: a bounded device-side wait gave up). The last error
@@ -61,7 +68,8 @@ typedef struct dn8_conv1_args {
     int32_t prologue_f16;
     /* 0: in0 / seg are the reference's group-major planes [G0][N*HW][32] / [G-G0][N*HW][32].
      * > 0: in0 is a tile-major block store [ceil(N*HW/128)][tile_groups][128][32] (128 consecutive
-     * pixels per tile, all of a tile's groups contiguous) holding groups 0 .. G-1; seg and G0 are unused. */
+     * pixels per tile, all of a tile's groups contiguous, bytes q + 128) holding groups 0 .. G-1; seg
+     * and G0 are unused. */
     int32_t tile_groups;
 } dn8_conv1_args;
 int dn8_conv1(const dn8_conv1_args* a, dn8_stream stream);
@@ -78,8 +86,8 @@ typedef struct dn8_conv2_args {
     int32_t* err;
     int32_t N, H, W;
     /* 0: out is the slot. > 0: out is a tile-major block store [ceil(N*H*W/128)][tile_groups][128][32]
-     * (128 consecutive pixels per tile, all of a tile's groups contiguous) and this layer writes its
-     * group `group` (< tile_groups). */
+     * (128 consecutive pixels per tile, all of a tile's groups contiguous, bytes q + 128) and this
+     * layer writes its group `group` (< tile_groups). */
     int32_t tile_groups, group;
 } dn8_conv2_args;
 int dn8_conv2(const dn8_conv2_args* a, dn8_stream stream);
@@ -100,11 +108,11 @@ typedef struct dn8_trans_args {
     int32_t* err;
     int32_t G0, G, N, H, W;
     int32_t prologue_f16;
-    /* > 0: in0 is a tile-major block store [ceil(N*H*W/128)][tile_groups][128][32] holding groups
-     * 0 .. G-1 (seg and G0 unused). */
+    /* > 0: in0 is a tile-major block store [ceil(N*H*W/128)][tile_groups][128][32] (bytes q + 128)
+     * holding groups 0 .. G-1 (seg and G0 unused). */
     int32_t tile_groups;
-    /* > 0: out is the next block's tile-major store [ceil(N*H*W/4/128)][out_tile_groups][128][32];
-     * the transition writes its groups 0 .. c_out/32 - 1. */
+    /* > 0: out is the next block's tile-major store [ceil(N*H*W/4/128)][out_tile_groups][128][32]
+     * (bytes q + 128); the transition writes its groups 0 .. c_out/32 - 1. */
     int32_t out_tile_groups;
 } dn8_trans_args;
 int dn8_trans(const dn8_trans_args* a, dn8_stream stream);
@@ -128,8 +136,8 @@ typedef struct dn8_stem_args {
     int32_t N, H, W;
     int32_t x_u8;
     int32_t n_alloc;       /* images the output groups are laid out for (>= N; 0 = N) */
-    /* > 0: out is block 1's tile-major store [ceil(n_alloc*H*W/16/128)][tile_groups][128][32]; the
-     * stem writes its groups 0 and 1. */
+    /* > 0: out is block 1's tile-major store [ceil(n_alloc*H*W/16/128)][tile_groups][128][32]
+     * (bytes q + 128); the stem writes its groups 0 and 1. */
     int32_t tile_groups;
 } dn8_stem_args;
 int dn8_stem(const dn8_stem_args* a, dn8_stream stream);
@@ -153,7 +161,7 @@ typedef struct dn8_head_args {
     int32_t G0, G, N, HW, n_out, per_view;
     int32_t n_alloc;        /* images the store groups are laid out for (>= N; 0 = N) */
     /* > 0: in0 is the last block's tile-major store [ceil(n_alloc*HW/128)][tile_groups][128][32]
-     * holding groups 0 .. G-1 (seg and G0 unused). */
+     * (bytes q + 128) holding groups 0 .. G-1 (seg and G0 unused). */
     int32_t tile_groups;
 } dn8_head_args;
 int dn8_head(const dn8_head_args* a, dn8_stream stream);
@@ -247,8 +255,9 @@ int dn8_engine_forward_to(dn8_engine* e, const dn8_input* in, int32_t n, int32_t
  * and overwrites what that kernel writes. No allocation, no synchronisation. */
 int dn8_engine_launch(dn8_engine* e, int32_t kind, int32_t block, int32_t layer, dn8_stream stream);
 /* Copies store segment j of block b (j = 0: the block input groups [G0][n][HW][32]; j >= 1: the
- * output of dense layer j-1, [n][HW][32]) to dst (device or host memory). Valid for the last two
- * blocks of the last pass (blocks alternate between two arenas). */
+ * output of dense layer j-1, [n][HW][32]) to dst (device or host memory) as signed q, enqueued on
+ * `stream` (a host dst holds the bytes once the stream has reached this point). Valid for the last
+ * two blocks of the last pass (blocks alternate between two arenas). */
 int dn8_engine_store(const dn8_engine* e, int32_t block, int32_t j, int8_t* dst, dn8_stream stream);
 /* One pass of n (<= pass size) images with a CUDA event after every launch (the reference's
  * `Dense8SEncoder.profile`, src/knee/dense8s.py:1548-1563): out[k] = kind, block, layer and device

@@ -205,6 +205,9 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
                          (in_r ? static_cast<int32_t>(r) : 0);
             }
         };
+        // the rounding add whose low byte is q (1.5 * 2^23), or q + 128 into a tile-major store
+        // (offset binary; the sum stays even, so ties still round to even q)
+        const float omag = a.tile_groups > 0 ? 12583040.0f : 12582912.0f;
         auto finish = [&](int t, const int32_t (&sum)[16]) {
             const int32_t* xq = xb + ((t % C2_XBUF) * 2 + ch) * 4 * 32;
             const bool ex_l = has_l && at_l, ex_r = has_r && at_r;
@@ -226,8 +229,8 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
                     const int32_t accv = sum[4 * j + k] + static_cast<int32_t>(le[k]) + static_cast<int32_t>(re[k]);
                     const float f = fast_cvt ? __int_as_float(accv + 0x4B400000) - 12582912.0f
                                              : __int2float_rn(accv);
-                    // rint(clamp(f sc, +-127)) as the low byte of (clamped + 1.5 * 2^23)
-                    q[k] = __float_as_uint(fminf(fmaxf(f * sc[k], -127.0f), 127.0f) + 12582912.0f);
+                    // rint(clamp(f sc, +-127)) (+ 128) as the low byte of (clamped + omag)
+                    q[k] = __float_as_uint(fminf(fmaxf(f * sc[k], -127.0f), 127.0f) + omag);
                 }
                 wd[j] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
             }

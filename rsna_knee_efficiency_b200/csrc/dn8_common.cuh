@@ -325,8 +325,8 @@ DN8_DEV uint32_t u32_of(__half2 h) {
     memcpy(&x, &h, 4);
     return x;
 }
-DN8_DEV uint32_t prologue_f16x4(uint32_t q4, uint32_t a01, uint32_t b01, uint32_t a23, uint32_t b23) {
-    const uint32_t w = q4 ^ 0x80808080u;                 // signed byte q -> unsigned q + 128
+// The store bytes in offset binary (each byte q + 128, the tile-major store's form).
+DN8_DEV uint32_t prologue_f16x4_ob(uint32_t w, uint32_t a01, uint32_t b01, uint32_t a23, uint32_t b23) {
     __half2 lo = h2_of(__byte_perm(w, 0x64646464u, 0x4140));   // fp16 pair 1024 + (q + 128)
     __half2 hi = h2_of(__byte_perm(w, 0x64646464u, 0x4342));
     const __half2 m1152 = h2_of(0xE480E480u), k255 = h2_of(0x5BF85BF8u), k1024 = h2_of(0x64006400u);
@@ -338,23 +338,27 @@ DN8_DEV uint32_t prologue_f16x4(uint32_t q4, uint32_t a01, uint32_t b01, uint32_
     hi = __hfma2(hi, k255, k1024);
     return __byte_perm(u32_of(lo), u32_of(hi), 0x6420);
 }
+// The store bytes as signed q (group-major planes, the reference's layout).
+DN8_DEV uint32_t prologue_f16x4(uint32_t q4, uint32_t a01, uint32_t b01, uint32_t a23, uint32_t b23) {
+    return prologue_f16x4_ob(q4 ^ 0x80808080u, a01, b01, a23, b23);   // signed q -> q + 128
+}
 
-// fp32 prologue of one store byte `q` (the reference's `pro16`, :99-120): v = sat(fmaf(a, q, b)),
-// u = rint(255 v) as the low byte of fmaf(v, 255, 2^23).
-DN8_DEV uint32_t prologue_f32(int q, float a, float b) {
-    const float f = __int_as_float(0x4B000000 | ((q + 128) & 0xFF)) - 8388736.0f;  // exact q
+// fp32 prologue of one store byte given as w = q + 128 (the reference's `pro16`, :99-120):
+// v = sat(fmaf(a, q, b)), u = rint(255 v) as the low byte of fmaf(v, 255, 2^23).
+DN8_DEV uint32_t prologue_f32(uint32_t w, float a, float b) {
+    const float f = __uint_as_float(0x4B000000u | w) - 8388736.0f;   // exact q
     const float v = __saturatef(fmaf(a, f, b));
     return __float_as_uint(fmaf(v, 255.0f, 8388608.0f)) & 0xFFu;
 }
-DN8_DEV uint32_t prologue_f32x4(uint32_t q4, const float2* ab) {
+// 4 store bytes in offset binary (q + 128 each)
+DN8_DEV uint32_t prologue_f32x4_ob(uint32_t w4, const float2* ab) {
     uint32_t r = 0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int q = static_cast<int>(static_cast<int8_t>((q4 >> (8 * k)) & 0xFF));
-        r |= prologue_f32(q, ab[k].x, ab[k].y) << (8 * k);
-    }
+    for (int k = 0; k < 4; ++k) r |= prologue_f32((w4 >> (8 * k)) & 0xFFu, ab[k].x, ab[k].y) << (8 * k);
     return r;
 }
+// 4 store bytes as signed q
+DN8_DEV uint32_t prologue_f32x4(uint32_t q4, const float2* ab) { return prologue_f32x4_ob(q4 ^ 0x80808080u, ab); }
 
 // Two fp16 pixels (one half2 word) -> two u8 in the low 16 bits: rint(255 sat(x)) computed in fp32
 // (the reference's `u8pair`, dense8s_kernels.cu:3631-3639).

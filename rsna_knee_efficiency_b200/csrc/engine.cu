@@ -465,6 +465,27 @@ int dn8_engine_check(dn8_engine* e, dn8_stream stream) {
     return DN8_OK;
 }
 
+}  // extern "C"
+
+// The engine's tile-major stores hold q + 128 per byte (offset binary): the copied segment is flipped
+// back to signed q in place, on the device, or on the host once the copy has landed.
+__global__ void store_to_signed_kernel(uint8_t* p, size_t n) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        p[i] ^= 0x80u;
+}
+struct HostFlip {
+    uint8_t* p;
+    size_t n;
+};
+static void CUDART_CB host_to_signed(void* arg) {
+    HostFlip* f = static_cast<HostFlip*>(arg);
+    for (size_t i = 0; i < f->n; ++i) f->p[i] ^= 0x80u;
+    delete f;
+}
+
+extern "C" {
+
 int dn8_engine_store(const dn8_engine* ec, int32_t block, int32_t j, int8_t* dst, dn8_stream stream) {
     dn8_engine* e = const_cast<dn8_engine*>(ec);
     if (e == nullptr || block < 0 || block >= e->n_blocks || j < 0 || j > e->L[block] || dst == nullptr)
@@ -485,6 +506,19 @@ int dn8_engine_store(const dn8_engine* ec, int32_t block, int32_t j, int8_t* dst
             ce = cudaMemcpy2DAsync(d, 4096, sg, static_cast<size_t>(Gt) * 4096, 4096, full, cudaMemcpyDefault, st);
         if (ce == cudaSuccess && rest > 0)
             ce = cudaMemcpyAsync(d + full * 4096, sg + full * Gt * 4096, rest * 32, cudaMemcpyDefault, st);
+    }
+    if (ce == cudaSuccess) {
+        const size_t bytes = static_cast<size_t>(ng) * rows * 32;
+        cudaPointerAttributes pa{};
+        ce = cudaPointerGetAttributes(&pa, dst);
+        if (ce == cudaSuccess && (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged)) {
+            store_to_signed_kernel<<<e->sms, 256, 0, st>>>(reinterpret_cast<uint8_t*>(dst), bytes);
+            ce = cudaGetLastError();
+        } else if (ce == cudaSuccess) {
+            HostFlip* f = new HostFlip{reinterpret_cast<uint8_t*>(dst), bytes};
+            ce = cudaLaunchHostFunc(st, host_to_signed, f);
+            if (ce != cudaSuccess) delete f;
+        }
     }
     return ce == cudaSuccess ? DN8_OK : efail(e, DN8_ECUDA, "store: %s", cudaGetErrorString(ce));
 }

@@ -135,9 +135,12 @@ static size_t gemm_layout(bool trans, bool pair, int G, int nc, int nchunks, int
     return used;
 }
 
-template <bool F16, bool TRANS, bool PAIR>
+template <bool F16, bool TRANS, bool PAIR, bool OB>
 __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
     using Cfg = GemmCfg<TRANS>;
+    // OB: the input store is tile-major and holds q + 128 per byte (offset binary), the prologue's
+    // own input form; group-major planes hold signed q, flipped to it by one xor per 4 bytes
+    constexpr uint32_t XM = OB ? 0u : 0x80808080u;
     constexpr int KSTEP = Cfg::KSTEP, SA = Cfg::SA;
     const int SR = TRANS ? GemmCfg<true>::SR : a.sr;            // transition: a fixed 4-stage ring
     constexpr int ASTAGE = UNITS * 4096;
@@ -464,24 +467,24 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                 if (F16) {
                     const uint4* tb = reinterpret_cast<const uint4*>(sTab + g * 128) + 2 * t0;
                     const uint4 ta = tb[0], tc = tb[1];          // channels 8 t0 .. + 3, + 4 .. + 7
-                    res[4 * x + 0] = prologue_f16x4(r0.x, ta.x, ta.y, ta.z, ta.w);
-                    res[4 * x + 1] = prologue_f16x4(r0.y, tc.x, tc.y, tc.z, tc.w);
-                    res[4 * x + 2] = prologue_f16x4(r1.x, ta.x, ta.y, ta.z, ta.w);
-                    res[4 * x + 3] = prologue_f16x4(r1.y, tc.x, tc.y, tc.z, tc.w);
-                    res[16 + 4 * x + 0] = prologue_f16x4(r2.x, ta.x, ta.y, ta.z, ta.w);
-                    res[16 + 4 * x + 1] = prologue_f16x4(r2.y, tc.x, tc.y, tc.z, tc.w);
-                    res[16 + 4 * x + 2] = prologue_f16x4(r3.x, ta.x, ta.y, ta.z, ta.w);
-                    res[16 + 4 * x + 3] = prologue_f16x4(r3.y, tc.x, tc.y, tc.z, tc.w);
+                    res[4 * x + 0] = prologue_f16x4_ob(r0.x ^ XM, ta.x, ta.y, ta.z, ta.w);
+                    res[4 * x + 1] = prologue_f16x4_ob(r0.y ^ XM, tc.x, tc.y, tc.z, tc.w);
+                    res[4 * x + 2] = prologue_f16x4_ob(r1.x ^ XM, ta.x, ta.y, ta.z, ta.w);
+                    res[4 * x + 3] = prologue_f16x4_ob(r1.y ^ XM, tc.x, tc.y, tc.z, tc.w);
+                    res[16 + 4 * x + 0] = prologue_f16x4_ob(r2.x ^ XM, ta.x, ta.y, ta.z, ta.w);
+                    res[16 + 4 * x + 1] = prologue_f16x4_ob(r2.y ^ XM, tc.x, tc.y, tc.z, tc.w);
+                    res[16 + 4 * x + 2] = prologue_f16x4_ob(r3.x ^ XM, ta.x, ta.y, ta.z, ta.w);
+                    res[16 + 4 * x + 3] = prologue_f16x4_ob(r3.y ^ XM, tc.x, tc.y, tc.z, tc.w);
                 } else {
                     const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32 + 8 * t0;
-                    res[4 * x + 0] = prologue_f32x4(r0.x, tb);
-                    res[4 * x + 1] = prologue_f32x4(r0.y, tb + 4);
-                    res[4 * x + 2] = prologue_f32x4(r1.x, tb);
-                    res[4 * x + 3] = prologue_f32x4(r1.y, tb + 4);
-                    res[16 + 4 * x + 0] = prologue_f32x4(r2.x, tb);
-                    res[16 + 4 * x + 1] = prologue_f32x4(r2.y, tb + 4);
-                    res[16 + 4 * x + 2] = prologue_f32x4(r3.x, tb);
-                    res[16 + 4 * x + 3] = prologue_f32x4(r3.y, tb + 4);
+                    res[4 * x + 0] = prologue_f32x4_ob(r0.x ^ XM, tb);
+                    res[4 * x + 1] = prologue_f32x4_ob(r0.y ^ XM, tb + 4);
+                    res[4 * x + 2] = prologue_f32x4_ob(r1.x ^ XM, tb);
+                    res[4 * x + 3] = prologue_f32x4_ob(r1.y ^ XM, tb + 4);
+                    res[16 + 4 * x + 0] = prologue_f32x4_ob(r2.x ^ XM, tb);
+                    res[16 + 4 * x + 1] = prologue_f32x4_ob(r2.y ^ XM, tb + 4);
+                    res[16 + 4 * x + 2] = prologue_f32x4_ob(r3.x ^ XM, tb);
+                    res[16 + 4 * x + 3] = prologue_f32x4_ob(r3.y ^ XM, tb + 4);
                 }
             }
             tmem_st16x256_2x4(tmem + tlane + TMEM_A_COL + sa * (UNITS * 8), res);
@@ -572,19 +575,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                     const uint4 t0 = tb[0], t1 = tb[1], t2 = tb[2], t3 = tb[3];    // 8 channel pairs (A, B)
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj) {
-                        res[jj].x = prologue_f16x4(q[jj].x, t0.x, t0.y, t0.z, t0.w);
-                        res[jj].y = prologue_f16x4(q[jj].y, t1.x, t1.y, t1.z, t1.w);
-                        res[jj].z = prologue_f16x4(q[jj].z, t2.x, t2.y, t2.z, t2.w);
-                        res[jj].w = prologue_f16x4(q[jj].w, t3.x, t3.y, t3.z, t3.w);
+                        res[jj].x = prologue_f16x4_ob(q[jj].x ^ XM, t0.x, t0.y, t0.z, t0.w);
+                        res[jj].y = prologue_f16x4_ob(q[jj].y ^ XM, t1.x, t1.y, t1.z, t1.w);
+                        res[jj].z = prologue_f16x4_ob(q[jj].z ^ XM, t2.x, t2.y, t2.z, t2.w);
+                        res[jj].w = prologue_f16x4_ob(q[jj].w ^ XM, t3.x, t3.y, t3.z, t3.w);
                     }
                 } else {
                     const float2* tb = reinterpret_cast<const float2*>(sTab) + g * 32 + h * 16;
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj) {
-                        res[jj].x = prologue_f32x4(q[jj].x, tb);
-                        res[jj].y = prologue_f32x4(q[jj].y, tb + 4);
-                        res[jj].z = prologue_f32x4(q[jj].z, tb + 8);
-                        res[jj].w = prologue_f32x4(q[jj].w, tb + 12);
+                        res[jj].x = prologue_f32x4_ob(q[jj].x ^ XM, tb);
+                        res[jj].y = prologue_f32x4_ob(q[jj].y ^ XM, tb + 4);
+                        res[jj].z = prologue_f32x4_ob(q[jj].z ^ XM, tb + 8);
+                        res[jj].w = prologue_f32x4_ob(q[jj].w ^ XM, tb + 12);
                     }
                 }
             }
@@ -608,6 +611,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
         // subtraction per channel pair; conv1's 255 v + 2^23 is one packed fma per pair as well).
         const int quad = warp & 3, half = (warp - 11) >> 2;
         const float4* gd4 = reinterpret_cast<const float4*>(sGd);
+        // transition: the rounding add whose low byte is q (1.5 * 2^23), or q + 128 for a tile-major
+        // output store (offset binary; the added 128 keeps the sum even, so ties still round to even q)
+        const float omag = a.tg_out > 0 ? 12583040.0f : 12582912.0f;
         // the conversion mode is fixed per launch: one instantiation of the tile loop per mode
         auto tiles = [&](auto fast_tag) {
             constexpr bool FAST = decltype(fast_tag)::value;
@@ -643,8 +649,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_kernel(const GemmArgs a) {
                             const float4 p = gdp[c >> 1];   // transition: (g0, d0, g1, d1); conv1: (g0, g1, d0, d1)
                             float2 r;
                             if (TRANS) {
-                                r.x = fminf(fmaxf(p.x * f.x, -127.0f), 127.0f) + 12582912.0f;
-                                r.y = fminf(fmaxf(p.z * f.y, -127.0f), 127.0f) + 12582912.0f;
+                                r.x = fminf(fmaxf(p.x * f.x, -127.0f), 127.0f) + omag;
+                                r.y = fminf(fmaxf(p.z * f.y, -127.0f), 127.0f) + omag;
                             } else {
                                 // sat(g acc + d) per channel (one rounding each), then 255 v + 2^23 on the pair
                                 r = __ffma2_rn(make_float2(__saturatef(fmaf(p.x, f.x, p.z)), __saturatef(fmaf(p.y, f.y, p.w))),
@@ -733,9 +739,9 @@ static int pair_slots(int sms) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaFuncSetAttribute(gemm_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_kernel<true, false, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BUDGET + 1024) != cudaSuccess ||
-        cudaOccupancyMaxActiveClusters(&n, gemm_kernel<true, false, true>, &cfg) != cudaSuccess || n <= 0) {
+        cudaOccupancyMaxActiveClusters(&n, gemm_kernel<true, false, true, true>, &cfg) != cudaSuccess || n <= 0) {
         (void)cudaGetLastError();
         n = sms / 2;
     }
@@ -748,8 +754,8 @@ static int pair_slots(int sms) {
 // (half the weights per CTA, resident for every layer of the network). Measured on B200 (same box):
 // single CTAs are 5-12 % faster where both fit; pairs are 8-10 % faster than single CTAs that stream
 // their weights.
-template <bool F16, bool TRANS>
-static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
+template <bool F16, bool TRANS, bool OB>
+static cudaError_t launch_gemm_ob(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
     bool pair = false;
     size_t smem = gemm_layout(TRANS, false, g.G, g.nc, g.nchunks, g.raw_bytes, &g.sb, &g.b_resident, &g.sr) + 1024;
     if (!TRANS && !g.b_resident) {
@@ -762,21 +768,26 @@ static cudaError_t launch_gemm(GemmArgs g, int sms, cudaStream_t st, bool pdl) {
     const int ntiles = ((g.rows + mt - 1) / mt) * g.nchunks;
     if (ntiles <= 0) return cudaSuccess;
     if (!pair) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, TRANS, false>,
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, TRANS, false, OB>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         const int grid = ntiles < sms ? ntiles : sms;
-        return launch_pdl(pdl, gemm_kernel<F16, TRANS, false>, dim3(grid), dim3(GM_THREADS), smem, st, g);
+        return launch_pdl(pdl, gemm_kernel<F16, TRANS, false, OB>, dim3(grid), dim3(GM_THREADS), smem, st, g);
     }
     if constexpr (!TRANS) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, false, true>,
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<F16, false, true, OB>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         const int slots = pair_slots(sms);
         const int pairs = ntiles < slots ? ntiles : slots;
-        return launch_pdl_pairs(pdl, gemm_kernel<F16, false, true>, dim3(2 * pairs), dim3(GM_THREADS), smem, st, g);
+        return launch_pdl_pairs(pdl, gemm_kernel<F16, false, true, OB>, dim3(2 * pairs), dim3(GM_THREADS), smem, st, g);
     }
     return cudaErrorInvalidConfiguration;
+}
+// a tile-major input store is offset binary (OB), group-major planes are signed
+template <bool F16, bool TRANS>
+static cudaError_t launch_gemm(const GemmArgs& g, int sms, cudaStream_t st, bool pdl) {
+    return g.tg > 0 ? launch_gemm_ob<F16, TRANS, true>(g, sms, st, pdl) : launch_gemm_ob<F16, TRANS, false>(g, sms, st, pdl);
 }
 
 // conv1 keeps every layer's weights resident: on single CTAs up to 37 K groups, on CTA pairs up to 70.

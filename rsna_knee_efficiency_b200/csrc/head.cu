@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
         // at tile p / 128, row p % 128)
         const int8_t* base;
         size_t tstride = 0, p0 = 0;
+        // the tile-major store holds q + 128 per byte already (offset binary); planes hold signed q
+        const uint32_t xm = a.tile_groups > 0 ? 0u : 0x80808080u;
         if (a.tile_groups > 0) {
             base = a.in0 + static_cast<size_t>(g) * 4096 + h * 16;
             tstride = static_cast<size_t>(a.tile_groups) << 12;
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__(HD_THREADS, 1) head_kernel(const dn8_head_args
             const size_t p = p0 + s;
             const int8_t* src = a.tile_groups > 0 ? base + (p >> 7) * tstride + (p & 127) * 32 : base + p * 32;
             const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
-            const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+            const uint32_t w[4] = {v.x ^ xm, v.y ^ xm, v.z ^ xm, v.w ^ xm};
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
                 // the byte q + 128 in the mantissa of 2^23: exact float q

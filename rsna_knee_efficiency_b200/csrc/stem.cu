@@ -462,13 +462,15 @@ stem_kernel(const dn8_stem_args a, const StemGeo geo) {
                                                 0x6420);
                         if (px < PW) {
                             // block 1 input, group-major [2][N][PH * PW][32] (this half is group hc), or
-                            // groups 0 / 1 of the tile-major block store
+                            // groups 0 / 1 of the tile-major block store, whose bytes are q + 128 (q <= 127:
+                            // the top bit set)
                             const size_t pix = (static_cast<size_t>(n) * PH + py) * PW + px;
-                            int8_t* dst = a.tile_groups > 0
-                                              ? a.out + (((pix >> 7) * a.tile_groups + hc) << 12) + (pix & 127) * 32
-                                              : a.out + hc * gstride + pix * 32;
-                            *reinterpret_cast<uint4*>(dst) = make_uint4(mx[0], mx[1], mx[2], mx[3]);
-                            *reinterpret_cast<uint4*>(dst + 16) = make_uint4(mx[4], mx[5], mx[6], mx[7]);
+                            const bool tiled = a.tile_groups > 0;
+                            const uint32_t ob = tiled ? 0x80808080u : 0u;
+                            int8_t* dst = tiled ? a.out + (((pix >> 7) * a.tile_groups + hc) << 12) + (pix & 127) * 32
+                                                : a.out + hc * gstride + pix * 32;
+                            *reinterpret_cast<uint4*>(dst) = make_uint4(mx[0] | ob, mx[1] | ob, mx[2] | ob, mx[3] | ob);
+                            *reinterpret_cast<uint4*>(dst + 16) = make_uint4(mx[4] | ob, mx[5] | ob, mx[6] | ob, mx[7] | ob);
                         }
                     }
                     __syncwarp();

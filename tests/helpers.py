@@ -55,20 +55,27 @@ def dev(a: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+def _flip(a: np.ndarray) -> np.ndarray:
+    """int8 q <-> its offset-binary byte q + 128 (the same bit flip both ways)."""
+    return (a.view(np.uint8) ^ np.uint8(0x80)).view(np.int8)
+
+
 def tile_major(X: np.ndarray, Gt: int | None = None) -> np.ndarray:
-    """Channel-last store X [N, HW, c] (c = 32 G) -> the tile-major block store
-    [ceil(N HW / 128), Gt, 128, 32] (groups G .. Gt - 1 and the rows past the last pixel zero)."""
+    """Channel-last store X [N, HW, c] (c = 32 G) of signed q -> the tile-major block store
+    [ceil(N HW / 128), Gt, 128, 32], whose bytes are q + 128 (offset binary; groups G .. Gt - 1 and
+    the rows past the last pixel zero bytes)."""
     N, HW, c = X.shape
     G = c // 32
     Gt = G if Gt is None else Gt
     rows = N * HW
     nt = -(-rows // 128)
     t = np.zeros((nt * 128, Gt, 32), np.int8)
-    t[:rows, :G] = X.reshape(rows, G, 32)
+    t[:rows, :G] = _flip(np.ascontiguousarray(X.reshape(rows, G, 32)))
     return np.ascontiguousarray(t.reshape(nt, 128, Gt, 32).transpose(0, 2, 1, 3))
 
 
 def from_tile_major(t: np.ndarray, rows: int, groups) -> np.ndarray:
-    """Tile-major [T, Gt, 128, 32] -> channel-last [rows, 32 len(groups)] of the given groups."""
+    """Tile-major [T, Gt, 128, 32] (bytes q + 128) -> channel-last signed q [rows, 32 len(groups)] of
+    the given groups."""
     flat = t.transpose(0, 2, 1, 3).reshape(-1, t.shape[1], 32)[:rows]
-    return np.ascontiguousarray(flat[:, list(groups)].reshape(rows, -1))
+    return _flip(np.ascontiguousarray(flat[:, list(groups)].reshape(rows, -1)))

@@ -10,7 +10,7 @@ import torch
 
 from oracle import oracle as orc
 from rsna_knee_efficiency_b200 import ops
-from tests.helpers import dev, pixels_to_planes, planes_to_pixels, plan_tables, rand_store, split_store
+from tests.helpers import dev, pixels_to_planes, planes_to_pixels, plan_tables, rand_store, split_store, tile_major
 
 pytestmark = pytest.mark.gpu
 
@@ -68,11 +68,8 @@ def test_conv1_tile_major_store(bi, li, N, HW):
     cin = c0 + 32 * li
     G, Gt = cin // 32, cin // 32 + 3
     rows = N * HW
-    nt = (rows + 127) // 128
     X = rand_store(np.random.default_rng(11 * bi + li), (N, HW, cin), "uniform").reshape(rows, cin)
-    tm = np.zeros((nt * 128, Gt, 32), dtype=np.int8)
-    tm[:rows, :G] = X.reshape(rows, G, 32)
-    tm = tm.reshape(nt, 128, Gt, 32).transpose(0, 2, 1, 3)
+    tm = tile_major(X.reshape(N, HW, cin), Gt)
     out = torch.full((8 * rows * 16,), 0xA5, dtype=torch.uint8, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     ops.conv1(dev(tm), None, dev(ops.prepare_conv1_weights(par[f"L{bi}_{li}_w1"])), dev(par[f"L{bi}_{li}_abh"]),
