@@ -121,6 +121,16 @@ def test_conv2_small_and_ragged(N, H, W):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("N,H,W", [(1, 1, 128), (3, 5, 128), (2, 100, 128), (300, 4, 128), (10, 128, 128)])
+def test_conv2_one_row_tiles(N, H, W):
+    """W = 128 (tiles of one image row, the block-1 geometry): one-row images (both vertical taps in
+    the zero padding), images of a few rows, and more tiles than CTAs so that CTAs take several
+    tiles across image boundaries."""
+    _, _, par = plan_tables(512)
+    got, want = _conv2_case(par, 1, 2, N, H, W, N * 1000 + H * 10 + W)
+    np.testing.assert_array_equal(got, want)
+
+
 def _trans_case(par, plan, bi, N, H, W, f16, kind, seed):
     rng = np.random.default_rng(seed)
     b = plan.blocks[bi]
