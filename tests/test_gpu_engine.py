@@ -168,6 +168,21 @@ def test_trace_matches_oracle_stores_and_time_layers_runs():
     assert set(stores) == set(tr)
     for key, t in tr.items():
         np.testing.assert_array_equal(stores[key].cpu().numpy().astype(np.int8), t, err_msg=str(key))
+    # dn8_engine_store into host memory (pinned, and pageable) gives the same signed bytes as into
+    # device memory: the tile-major store's offset-binary bytes are flipped back on either side
+    import ctypes
+    from rsna_knee_efficiency_b200 import _native as nat
+    last = len(enc.meta["blocks"]) - 1
+    want_seg = tr[(last, 1)].reshape(-1)
+    pinned = torch.empty(want_seg.size, dtype=torch.int8, pin_memory=True)
+    pageable = np.empty(want_seg.size, np.int8)
+    for ptr in (pinned.data_ptr(), pageable.ctypes.data):
+        nat.check(nat.lib().dn8_engine_store(enc._h, last, 1, ctypes.c_void_p(ptr), enc.stream.cuda_stream),
+                  "dn8_engine_store", enc._h)
+    enc.stream.synchronize()
+    dev_seg = stores[(last, 1)].cpu().numpy().astype(np.int8)      # [n][c][h][w] from the device path
+    for got in (pinned.numpy(), pageable):
+        np.testing.assert_array_equal(got.reshape(n, -1, 32).transpose(0, 2, 1).reshape(dev_seg.shape), dev_seg)
     times = enc.time_layers(reps=3)
     blocks = enc.meta["blocks"]
     assert len(times) == sum(2 * b["L"] for b in blocks) + sum(1 for b in blocks if b["trans"])
