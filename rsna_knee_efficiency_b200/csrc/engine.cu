@@ -19,6 +19,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <new>
+
 #include "dn8_kernels.h"
 
 struct dn8_engine {
@@ -89,7 +91,9 @@ void dn8_engine_destroy(dn8_engine* e) {
     delete e;
 }
 
-int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
+}  // extern "C"
+
+static int engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
     if (out == nullptr || p == nullptr) return DN8_EINVAL;
     *out = nullptr;
     dn8_engine* e = new dn8_engine();
@@ -273,6 +277,18 @@ int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
     cudaSetDevice(prev);
     *out = e;
     return DN8_OK;
+}
+
+extern "C" {
+
+// host allocation failures (std::bad_alloc) end as a status, not as an exception through the C ABI
+int dn8_engine_create(const dn8_pack_desc* p, int device, dn8_engine** out) {
+    try {
+        return engine_create(p, device, out);
+    } catch (const std::exception& ex) {
+        dn8::set_last_error(ex.what());
+        return DN8_EINVAL;
+    }
 }
 
 // In profiling mode, records an event after a launch of (kind, block, layer).
@@ -515,8 +531,8 @@ int dn8_engine_store(const dn8_engine* ec, int32_t block, int32_t j, int8_t* dst
             store_to_signed_kernel<<<e->sms, 256, 0, st>>>(reinterpret_cast<uint8_t*>(dst), bytes);
             ce = cudaGetLastError();
         } else if (ce == cudaSuccess) {
-            HostFlip* f = new HostFlip{reinterpret_cast<uint8_t*>(dst), bytes};
-            ce = cudaLaunchHostFunc(st, host_to_signed, f);
+            HostFlip* f = new (std::nothrow) HostFlip{reinterpret_cast<uint8_t*>(dst), bytes};
+            ce = f == nullptr ? cudaErrorMemoryAllocation : cudaLaunchHostFunc(st, host_to_signed, f);
             if (ce != cudaSuccess) delete f;
         }
     }
