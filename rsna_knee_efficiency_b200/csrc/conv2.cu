@@ -21,7 +21,10 @@
 
 namespace dn8 {
 
-constexpr int C2_STAGES = 3;
+// Input ring depth: 5 stages where they fit (maps up to 64 x 64: a tile's MMAs are short there, so
+// the loads have to run further ahead; -6 % at 32 x 32), else 3 (128 x 128: 48 KB stages). A
+// compile-time depth per kernel instance keeps the ring arithmetic constant.
+constexpr int C2_STAGES_DEEP = 5, C2_STAGES = 3;
 constexpr int C2_THREADS = 576;
 constexpr int C2_W_BYTES = 36864;            // [dy][cblk][2 halves][96 rows][16 B]
 constexpr int C2_XBUF = 4;                   // edge-exchange buffers (tile t uses t % 4: one group's)
@@ -38,23 +41,29 @@ static inline size_t c2_stage_bytes(int Rt, int W) {
     const size_t b = need > 8 * pl ? need : 8 * pl;
     return ((b + 1023) / 1024) * 1024;
 }
+static inline size_t c2_smem_for(int ns, size_t stage) {
+    return 1024 + C2_W_BYTES + ns * stage + 128 + C2_XBUF * 2 * 4 * 2 * 16 * 4 + 8 * (2 * ns + 5 + 2 * C2_XBUF) + 16;
+}
+static inline int c2_stages(int H, int W) {
+    return c2_smem_for(C2_STAGES_DEEP, c2_stage_bytes(c2_rows_per_tile(H, W), W)) <= 227 * 1024 ? C2_STAGES_DEEP
+                                                                                                  : C2_STAGES;
+}
 size_t conv2_smem_bytes(int H, int W) {
-    const int Rt = c2_rows_per_tile(H, W);
-    return 1024 + C2_W_BYTES + C2_STAGES * c2_stage_bytes(Rt, W) + 128 + C2_XBUF * 2 * 4 * 2 * 16 * 4 +
-           8 * (2 * C2_STAGES + 5 + 2 * C2_XBUF) + 16;
+    return c2_smem_for(c2_stages(H, W), c2_stage_bytes(c2_rows_per_tile(H, W), W));
 }
 
+template <int NS>
 __global__ void __launch_bounds__(C2_THREADS, 1)
 conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, int Rt, uint32_t stage_bytes) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
     uint8_t* sX = smem + C2_W_BYTES;                       // stages, 1024-aligned (36864 = 36 * 1024)
-    float* sSc = reinterpret_cast<float*>(sX + C2_STAGES * stage_bytes);
+    float* sSc = reinterpret_cast<float*>(sX + NS * stage_bytes);
     int32_t* xb = reinterpret_cast<int32_t*>(sSc + 32);    // [XBUF][2 ch][4 quad][2][16]
     uint64_t* full = reinterpret_cast<uint64_t*>(xb + C2_XBUF * 2 * 4 * 2 * 16);
-    uint64_t* empty = full + C2_STAGES;
-    uint64_t* accf = empty + C2_STAGES;
+    uint64_t* empty = full + NS;
+    uint64_t* accf = empty + NS;
     uint64_t* acce = accf + 2;
     uint64_t* xbar = acce + 2;                             // [XBUF][2 ch]: neighbour exchange
     uint64_t* wfull = xbar + 2 * C2_XBUF;
@@ -69,7 +78,7 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
     const uint32_t PL = static_cast<uint32_t>((Rt + 2) * W * 16);     // one plane of a stage
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C2_STAGES; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -108,8 +117,8 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         // ---------------- TMA producer ----------------
         if (lane == 0 && my_tiles > 0) {
             for (int t = 0; t < my_tiles; ++t) {
-                const int s = t % C2_STAGES;
-                if (!mbar_wait(&empty[s], ((t / C2_STAGES) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (33 << 4))) break;
+                const int s = t % NS;
+                if (!mbar_wait(&empty[s], ((t / NS) & 1) ^ 1, a.err, s_abort, ERR_WAIT_EMPTY | (33 << 4))) break;
                 const int tile = blockIdx.x + t * gridDim.x;
                 const int n = tile / tpi, y0 = (tile - n * tpi) * Rt;
                 mbar_expect_tx(&full[s], 8u * PL);
@@ -123,10 +132,10 @@ conv2_kernel(const __grid_constant__ CUtensorMap tmap, const dn8_conv2_args a, i
         const uint32_t x0 = smem_u32(sX), w0 = smem_u32(sW);
         const bool wok = my_tiles == 0 || mbar_wait_w(&wfull[0], 0, a.err, s_abort, ERR_WAIT_FULL | (34 << 4));
         for (int t = 0; t < my_tiles && wok; ++t) {
-            const int acc = t & 1, s = t % C2_STAGES;
+            const int acc = t & 1, s = t % NS;
             if (!mbar_wait_w(&acce[acc], ((t >> 1) & 1) ^ 1, a.err, s_abort, ERR_WAIT_ACC | (35 << 4))) break;
             tc_fence_after();
-            if (!mbar_wait_w(&full[s], (t / C2_STAGES) & 1, a.err, s_abort, ERR_WAIT_FULL | (36 << 4))) break;
+            if (!mbar_wait_w(&full[s], (t / NS) & 1, a.err, s_abort, ERR_WAIT_FULL | (36 << 4))) break;
             tc_fence_after();
             const uint32_t xs = x0 + s * stage_bytes;
 #pragma unroll
@@ -308,10 +317,10 @@ cudaError_t launch_conv2(const Conv2Plan& plan, const dn8_conv2_args& a, int sms
     const int ntiles = a.N * tpi;
     const int grid = ntiles < sms ? ntiles : sms;
     if (grid <= 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(conv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(plan.smem));
+    const auto kernel = c2_stages(a.H, a.W) == C2_STAGES_DEEP ? conv2_kernel<C2_STAGES_DEEP> : conv2_kernel<C2_STAGES>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem));
     if (e != cudaSuccess) return e;
-    return launch_pdl(pdl, conv2_kernel, dim3(grid), dim3(C2_THREADS), plan.smem, st, plan.map, a, plan.Rt,
+    return launch_pdl(pdl, kernel, dim3(grid), dim3(C2_THREADS), plan.smem, st, plan.map, a, plan.Rt,
                       plan.stage_bytes);
 }
 
